@@ -1,0 +1,546 @@
+"""Benchmark of the b200 non-GEMM op path: the row-sharded Llama-3-8B-shaped stack.
+
+Workload (one "step"): 32 decoder layers of the non-GEMM chain
+  RMSNorm(hidden 4096, eps 1e-5) -> RoPE on q [T,32,128] / k [T,8,128]
+  (theta 1e4, global positions) -> SwiGLU (intermediate 14336) -> residual add
+over 131072 bf16 tokens split by rows across the ranks (no collective on the
+hot path).  Activations ~ N(0,1), weights ~ 1 + N(0,0.1), per-layer weights
+seeded 1000*layer + tensor id; one activation set per rank is reused by all
+layers (the bytes moved are the same as with fresh activations per layer).
+
+Outputs ONE JSON line (rank 0):
+  value     tokens/s of the whole job, inputs resident in HBM, device time
+            (CUDA events), max over ranks.
+  e2e       the same metric through the public API with the hidden state
+            copied host->device before and device->host after every step.
+  roofline  the dominant kernel (SwiGLU + residual add) against the measured
+            HBM copy bandwidth.
+  per_op    achieved HBM GB/s of every kernel of the step (CUDA events
+            around each launch inside the timed region).
+  cpu_baseline  the reference's CPU path (HF formulas on torch CPU aten) on
+            a bounded sample, rank 0 at N=1.
+
+`--impl reference` times the reference's own CPU implementation of the path
+(the same HF formulas on torch CPU aten, all host threads) on a bounded
+sample and prints the same metric with "impl": "reference".
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "pytorch-plugin-fl_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+HIDDEN, HQ, HKV, HEAD, INTER = 4096, 32, 8, 128, 14336
+EPS, THETA = 1e-5, 10000.0
+BF16 = 2
+# Algorithmic HBM bytes per token per layer (every input read once, every
+# output written once):
+BYTES = {
+    "rms_norm": 2 * HIDDEN * BF16,                          # x in, out
+    "rope_qk": 2 * (HQ + HKV) * HEAD * BF16,                # q,k in and out
+    "swiglu": 3 * INTER * BF16,                             # gate, up in; act out
+    "residual_add": 3 * HIDDEN * BF16,                      # x, y in; h out
+}
+BYTES["swiglu_residual"] = BYTES["swiglu"] + BYTES["residual_add"]
+BYTES_PER_TOKEN_LAYER = BYTES["rms_norm"] + BYTES["rope_qk"] + BYTES["swiglu_residual"]
+TABLE_BYTES_PER_TOKEN = 2 * HEAD * BF16                     # cos/sin rows (cached)
+
+WORKLOAD = ("Llama-3-8B-shaped non-GEMM stack: 32 layers x [RMSNorm(4096) -> RoPE(q 32x128, "
+            "k 8x128) -> SwiGLU(14336) -> residual add], bf16, tokens split by rows")
+
+
+def _env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def committed_traffic():
+    """Per-token DRAM bytes of the dominant kernel from the committed ncu
+    summary (profiles/traffic.json), or None."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"fl_b200_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        try:
+            os.remove(self.path)
+        except OSError:
+            pass
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- the stack
+class Stack:
+    """Device-resident buffers of one rank's row shard and the launch list."""
+
+    def __init__(self, tokens, layers, pos0, device, rounding, fuse_add_norm):
+        from torch_fl import kernels as K
+
+        self.K = K
+        self.T, self.L, self.dev = tokens, layers, device
+        self.rounding = rounding
+        self.fuse = fuse_add_norm
+        rank = _env_int("RANK", 0)
+        g = torch.Generator(device=device)
+
+        def rn(seed, *shape, scale=1.0, loc=0.0):
+            g.manual_seed(seed + 100000 * rank)
+            return (loc + scale * torch.randn(*shape, generator=g, device=device)).to(torch.bfloat16)
+
+        T = tokens
+        self.x0 = rn(1, T, HIDDEN)
+        self.q = rn(2, 1, T, HQ, HEAD)
+        self.k = rn(3, 1, T, HKV, HEAD)
+        self.g = rn(4, T, INTER)
+        self.u = rn(5, T, INTER)
+        self.y = rn(6, T, HIDDEN)
+        self.w = [rn(1000 * l + 7, HIDDEN, scale=0.1, loc=1.0) for l in range(layers)]
+        # RoPE tables for the rank's global positions (HF construction, fp32 -> bf16)
+        pos = torch.arange(pos0, pos0 + T, device=device, dtype=torch.float32)
+        inv = 1.0 / (THETA ** (torch.arange(0, HEAD, 2, device=device, dtype=torch.float32) / HEAD))
+        fr = pos[:, None] * inv[None, :]
+        emb = torch.cat([fr, fr], dim=-1)
+        self.cos, self.sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+        self.pos0 = pos0
+        # outputs (reused by every layer)
+        self.xa = torch.empty_like(self.x0)
+        self.xb = torch.empty_like(self.x0)
+        self.n = torch.empty_like(self.x0)
+        self.qo = torch.empty_like(self.q)
+        self.ko = torch.empty_like(self.k)
+        self.a = torch.empty_like(self.g)
+
+    def launches_per_step(self):
+        return (3 * self.L + 1) if self.fuse else 3 * self.L
+
+    def run(self, x_in, timer=None):
+        """One step over all layers; returns the final hidden state buffer.
+        timer(name) returns a context manager that brackets one launch."""
+        K, r = self.K, self.rounding
+        x, nxt = x_in, self.xa
+        def t(name):
+            return timer(name) if timer else _null
+        if self.fuse:
+            with t("rms_norm"):
+                K.rms_norm(x, self.w[0], EPS, rounding=r, out=self.n)
+        for l in range(self.L):
+            if not self.fuse:
+                with t("rms_norm"):
+                    K.rms_norm(x, self.w[l], EPS, rounding=r, out=self.n)
+            with t("rope_qk"):
+                self._rope()
+            if self.fuse and l + 1 < self.L:
+                with t("swiglu"):
+                    K.swiglu(self.g, self.u, rounding=r, out=self.a)
+                with t("add_rms_norm"):
+                    K.add_rms_norm(x, self.y, self.w[l + 1], EPS, rounding=r, h_out=nxt, out=self.n)
+            else:
+                with t("swiglu_residual"):
+                    K.swiglu_residual(self.g, self.u, x, self.y, rounding=r, act_out=self.a, h_out=nxt)
+            x, nxt = nxt, (self.xb if nxt is self.xa else self.xa)
+        return x
+
+    def _rope(self):
+        self.K.rope_qk(self.q, self.k, self.cos, self.sin, layout="bshd", rounding=self.rounding,
+                       q_out=self.qo, k_out=self.ko)
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+_null = _Null()
+
+
+class EventTimer:
+    """Brackets launches with CUDA events on the current stream."""
+
+    def __init__(self):
+        self.ev = {}
+
+    def __call__(self, name):
+        timer = self
+
+        class _Ctx:
+            def __enter__(self_):
+                self_.s = torch.cuda.Event(enable_timing=True)
+                self_.e = torch.cuda.Event(enable_timing=True)
+                self_.s.record()
+                return self_
+
+            def __exit__(self_, *a):
+                self_.e.record()
+                timer.ev.setdefault(name, []).append((self_.s, self_.e))
+                return False
+
+        return _Ctx()
+
+    def mean_ms(self):
+        return {k: sum(s.elapsed_time(e) for s, e in v) / len(v) for k, v in self.ev.items()}
+
+    def counts(self):
+        return {k: len(v) for k, v in self.ev.items()}
+
+
+# ----------------------------------------------------------- CPU reference
+def cpu_reference(sample_tokens, reps, threads):
+    """The reference's own CPU path on a bounded sample: one decoder layer's
+    chain on `sample_tokens` tokens, HF formulas over torch CPU aten.  Returns
+    (seconds per token-layer, description)."""
+    from oracle import hf_chain
+
+    torch.set_num_threads(threads)
+    T = sample_tokens
+    g = torch.Generator().manual_seed(0)
+    bf = torch.bfloat16
+
+    def rn(*s, scale=1.0, loc=0.0):
+        return (loc + scale * torch.randn(*s, generator=g)).to(bf)
+
+    x, y, w = rn(T, HIDDEN), rn(T, HIDDEN), rn(HIDDEN, scale=0.1, loc=1.0)
+    q = rn(1, T, HQ, HEAD).transpose(1, 2)
+    k = rn(1, T, HKV, HEAD).transpose(1, 2)
+    gt, up = rn(T, INTER), rn(T, INTER)
+    cos, sin = hf_chain.rope_tables(torch.arange(T)[None], HEAD, THETA, bf)
+    hf_chain.decoder_chain(x[:64], w, q[:, :, :64], k[:, :, :64], cos[:, :64], sin[:, :64],
+                           gt[:64], up[:64], y[:64], EPS)   # warm-up
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        hf_chain.decoder_chain(x, w, q, k, cos, sin, gt, up, y, EPS)
+        times.append(time.perf_counter() - t0)
+    per = statistics.median(times) / T
+    desc = (f"HF formulas (modeling_qwen3.py RMSNorm/apply_rotary_pos_emb/silu*up) + add on torch "
+            f"{torch.__version__} CPU aten, one decoder layer x {T} tokens, median of {reps}; "
+            f"scaled to the 32-layer stack")
+    return per, desc
+
+
+def cpu_info():
+    model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return model
+
+
+# --------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--tokens", type=int, default=131072)
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--rounding", default="fused", choices=["fused", "chain"])
+    ap.add_argument("--no-fuse-add-norm", action="store_true")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=2048)
+    ap.add_argument("--cpu-reps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    assert args.warmup >= 3 or os.environ.get("FL_B200_BENCH_ALLOW_SHORT"), "use --warmup >= 3"
+
+    world = _env_int("WORLD_SIZE", 1)
+    rank = _env_int("RANK", 0)
+    local = _env_int("LOCAL_RANK", 0)
+    threads = os.cpu_count() or 1
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        reps = max(args.steps, 1)
+        per, desc = cpu_reference(args.cpu_sample_tokens, reps, threads)
+        value = 1.0 / (per * args.layers)
+        line = {"metric": "fused-layer tokens/s", "value": value, "unit": "tokens/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": per * args.tokens * args.layers * 1e3, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "impl": "reference",
+                "config": {"workload": WORKLOAD, "tokens": args.tokens, "layers": args.layers,
+                           "hidden": HIDDEN, "intermediate": INTER, "heads": [HQ, HKV, HEAD]},
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads,
+                                 "kind": "reference", "sample": desc, "cpu": cpu_info()},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    import torch_fl  # noqa: F401  (loads libfl_b200.so; fails loudly if missing)
+    from torch_fl import kernels as K
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    T = args.tokens // world
+    assert T * world == args.tokens, "tokens must split evenly across ranks"
+    stack = Stack(T, args.layers, rank * T, dev, args.rounding, not args.no_fuse_add_norm)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # warm-up
+    for _ in range(args.warmup):
+        stack.run(stack.x0)
+    barrier()
+
+    # timed region: device time with events on the launching stream
+    clocks = ClockSampler(local)
+    clocks.start()
+    timer = EventTimer()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    start.record()
+    for _ in range(args.steps):
+        out = stack.run(stack.x0, timer)
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    clock_info = clocks.stop()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = args.tokens * args.steps / (ms / 1e3)
+
+    kern_ms = timer.mean_ms()
+    counts = timer.counts()
+    per_op = {}
+    bytes_of = dict(BYTES)
+    bytes_of["add_rms_norm"] = 4 * HIDDEN * BF16
+    for name, m in kern_ms.items():
+        b = bytes_of[name] * T
+        per_op[name] = {"ms": round(m, 4), "gbs": round(b / (m * 1e-3) / 1e9, 1),
+                        "launches": counts[name]}
+    dom = "swiglu_residual" if "swiglu_residual" in kern_ms else "swiglu"
+    dom_bytes = bytes_of[dom] * T
+    achieved = dom_bytes / (kern_ms[dom] * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+    traffic = None
+    tj = committed_traffic()
+    if tj and dom in tj.get("bytes_per_token", {}):
+        traffic = tj["bytes_per_token"][dom] * T
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                else "fallback", "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "traffic": traffic, "algorithmic_bytes": dom_bytes}
+
+    # end to end through the public API, host buffers, copies inside the timed region
+    e2e = None
+    if not args.no_e2e:
+        h_in = torch.empty(T, HIDDEN, dtype=torch.bfloat16, pin_memory=True)
+        h_in.copy_(stack.x0)
+        h_out = torch.empty_like(h_in, pin_memory=True)
+        d_in = torch.empty_like(stack.x0)
+        for _ in range(2):
+            d_in.copy_(h_in, non_blocking=True)
+            h_out.copy_(stack.run(d_in), non_blocking=True)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            d_in.copy_(h_in, non_blocking=True)
+            res = stack.run(d_in)
+            h_out.copy_(res, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        ems = e0.elapsed_time(e1)
+        if world > 1:
+            import torch.distributed as dist
+
+            t = torch.tensor([ems], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        nbytes = h_in.numel() * h_in.element_size()
+        e2e = {"value": args.tokens * args.steps / (ems / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+               "ms_per_step": ems / args.steps,
+               "api": "torch_fl.kernels (C ABI of libfl_b200.so) on device tensors"}
+
+    # correctness gather (NCCL, outside the timed region): sampled rows of
+    # every rank checked on rank 0 against the oracle
+    check = correctness_sample(stack, K, world, rank, dev)
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            per, desc = cpu_reference(args.cpu_sample_tokens, args.cpu_reps, threads)
+            cpu = {"value": 1.0 / (per * args.layers), "unit": "tokens/s", "cores": threads,
+                   "kind": "reference", "sample": desc, "cpu": cpu_info()}
+        line = {
+            "metric": "fused-layer tokens/s", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "tokens": args.tokens, "tokens_per_rank": T,
+                       "layers": args.layers, "hidden": HIDDEN, "intermediate": INTER,
+                       "heads": [HQ, HKV, HEAD], "rounding": args.rounding,
+                       "fused_add_rms_norm": not args.no_fuse_add_norm,
+                       "parallelism": f"rows/{world}",
+                       "l2": "inputs larger than L2 (every per-rank activation >= 256 MB)"},
+            "hbm_gbs_step": round(stack_bytes(stack) * args.steps / (ms / 1e3) / 1e9, 1),
+            "per_op": per_op, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": stack.launches_per_step() * args.steps,
+            "clocks": clock_info, "correctness": check,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def stack_bytes(stack):
+    """Algorithmic HBM bytes of one step on this rank."""
+    T, L = stack.T, stack.L
+    if stack.fuse:
+        per = BYTES["rope_qk"] + BYTES["swiglu"]
+        return T * (L * per + BYTES["rms_norm"] + (L - 1) * 4 * HIDDEN * BF16 + BYTES["residual_add"])
+    return T * L * BYTES_PER_TOKEN_LAYER
+
+
+def correctness_sample(stack, K, world, rank, dev):
+    """Gather 4 rows of every rank's first-layer outputs to rank 0 and check
+    them against the oracle (RoPE rows carry the global positions)."""
+    rows = torch.tensor([0, 1, stack.T // 2, stack.T - 1], device=dev)
+    n = K.rms_norm(stack.x0, stack.w[0], EPS, rounding=stack.rounding)
+    stack._rope()
+    a, h = K.swiglu_residual(stack.g, stack.u, stack.x0, stack.y, rounding=stack.rounding)
+    parts = [stack.x0[rows], stack.y[rows], n[rows], stack.g[rows], stack.u[rows], a[rows], h[rows],
+             stack.q[0, rows].reshape(4, -1), stack.qo[0, rows].reshape(4, -1)]
+    flat = torch.cat([p.reshape(-1) for p in parts])
+    if world > 1:
+        import torch.distributed as dist
+
+        out = torch.empty(world * flat.numel(), dtype=flat.dtype, device=dev)
+        dist.all_gather_into_tensor(out, flat)
+        gathered = out.view(world, -1)
+    else:
+        gathered = flat.view(1, -1)
+    if rank != 0:
+        return None
+    import numpy as np
+
+    from oracle import ops
+
+    worst = 0
+    sizes = [p.numel() for p in parts]
+    w0 = stack.w[0].float().cpu().numpy()
+    for r in range(world):
+        vals = torch.split(gathered[r].float().cpu(), sizes)
+        x, y, nn, g, u, a_, h_, q, qo = [v.numpy().reshape(4, -1) for v in vals]
+        pos = r * stack.T + np.array([0, 1, stack.T // 2, stack.T - 1])
+        ct, st = ops.rope_tables(pos, HEAD, THETA, "bf16")
+        checks = [
+            (nn, ops.rms_norm_golden(x, w0, EPS, "bf16") if stack.rounding == "fused"
+             else ops.rms_norm_chain(x, w0, EPS, "bf16")),
+            (a_, ops.swiglu_golden(g, u, "bf16") if stack.rounding == "fused"
+             else ops.swiglu_chain(g, u, "bf16")),
+            (h_, ops.add_golden(x, y, 1.0, "bf16")),
+        ]
+        qref = (ops.rope_golden if stack.rounding == "fused" else ops.rope_chain)(
+            q.reshape(4, HQ, HEAD), ct[:, None], st[:, None], "bf16").reshape(4, -1)
+        checks.append((qo, qref))
+        for got, ref in checks:
+            worst = max(worst, int(ops.ulp_diff(got, ref, "bf16").max()))
+    return {"max_ulp_vs_oracle": worst, "ranks_checked": world, "ok": worst <= 1}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,204 @@
+// RMSNorm forward and fused residual-add + RMSNorm.
+//
+// Reference behaviour: the HF formula (transformers
+// models/qwen3/modeling_qwen3.py:59-64) run op by op on the flagos device:
+//   h32 = x.to(f32); var = h32.pow(2).mean(-1, keepdim); h = h32*rsqrt(var+eps)
+//   out = w * h.to(x.dtype)
+// i.e. csrc/aten/backends/cuda/{pow.cu:29-32, mean.cu:30-63, add.cu:72-76,
+// rsqrt.cu:14-32, mul.cu:28-52} plus two _to_copy casts
+// (csrc/aten/copy_ops.cc:225-240).  Here it is one pass: each row is read
+// once into registers, reduced in fp32, scaled and written once.
+#include "row_ladder.cuh"
+
+namespace flb200 {
+namespace {
+
+// out = w * (x * r) with r = 1/sqrt(mean(x^2) + eps).  In chain mode the
+// product x*r is rounded to T before the weight multiply, as the HF
+// `.to(input_dtype)` does.
+template <typename T, bool CHAIN>
+__device__ __forceinline__ void rms_scale_store(const uint4& xv, const T* w, T* o,
+                                                float r) {
+  constexpr int VW = Elem<T>::kVec;
+  float f[VW], wf[VW], y[VW];
+  unpack<T>(xv, f);
+  unpack<T>(ld_cached(w), wf);
+#pragma unroll
+  for (int e = 0; e < VW; ++e) {
+    float t = f[e] * r;
+    if (CHAIN) t = round_to<T>(t);
+    y[e] = wf[e] * t;
+  }
+  st_stream(o, pack<T>(y));
+}
+
+// Row-in-registers kernel: TPR threads own a row, VPT packs each.
+// If ADD, the row is h = x + y (rounded to T, stored to h) and the norm is
+// taken over h.
+template <typename T, int TPR, int VPT, int BLOCK, bool CHAIN, bool ADD>
+__global__ void __launch_bounds__(BLOCK, ladder_min_blocks<BLOCK>())
+rms_norm_vec_kernel(const T* x, int64_t ldx, const T* y, T* h, const T* w, T* out,
+                    int64_t ldo, int64_t rows, int nvec, float eps, float cols_f) {
+  constexpr int VW = Elem<T>::kVec;
+  constexpr int RPB = BLOCK / TPR;
+  __shared__ float smem[BLOCK / 32];
+  const int slot = threadIdx.x / TPR;
+  const int lane = threadIdx.x % TPR;
+  for (int64_t base = (int64_t)blockIdx.x * RPB; base < rows;
+       base += (int64_t)gridDim.x * RPB) {
+    const int64_t row = base + slot;
+    const bool ok = row < rows;
+    const T* xr = x + row * ldx;
+    uint4 v[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = lane + i * TPR;
+      v[i] = (ok && vi < nvec) ? ld_stream(xr + (int64_t)vi * VW) : make_uint4(0, 0, 0, 0);
+    }
+    if constexpr (ADD) {
+      const T* yr = y + row * ldx;
+      T* hr = h + row * ldx;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int vi = lane + i * TPR;
+        if (ok && vi < nvec) {
+          float a[VW], b[VW];
+          unpack<T>(v[i], a);
+          unpack<T>(ld_stream(yr + (int64_t)vi * VW), b);
+#pragma unroll
+          for (int e = 0; e < VW; ++e) a[e] = a[e] + b[e];
+          v[i] = pack<T>(a);  // the residual stream is stored in T
+          st_stream(hr + (int64_t)vi * VW, v[i]);
+        }
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      float f[VW];
+      unpack<T>(v[i], f);
+#pragma unroll
+      for (int e = 0; e < VW; ++e) ss = fmaf(f[e], f[e], ss);
+    }
+    ss = row_reduce<SumOp, TPR, BLOCK>(ss, smem);
+    const float r = 1.0f / sqrtf(ss / cols_f + eps);
+    T* orow = out + row * ldo;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = lane + i * TPR;
+      if (ok && vi < nvec)
+        rms_scale_store<T, CHAIN>(opaque(v[i]), w + (int64_t)vi * VW, orow + (int64_t)vi * VW, r);
+    }
+  }
+}
+
+// Looped kernel for any row length and alignment: one CTA per row, scalar
+// element loads; the row is read twice (the second read mostly hits L2).
+template <typename T, bool CHAIN, bool ADD>
+__global__ void __launch_bounds__(256)
+rms_norm_loop_kernel(const T* x, int64_t ldx, const T* y, T* h, const T* w, T* out,
+                     int64_t ldo, int64_t rows, int64_t cols, float eps) {
+  __shared__ float smem[256 / 32];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const T* xr = x + row * ldx;
+    float ss = 0.f;
+    for (int64_t c = threadIdx.x; c < cols; c += 256) {
+      float f = Elem<T>::to_f(xr[c]);
+      if constexpr (ADD) {
+        f = round_to<T>(f + Elem<T>::to_f(y[row * ldx + c]));
+        h[row * ldx + c] = Elem<T>::from_f(f);
+      }
+      ss = fmaf(f, f, ss);
+    }
+    ss = block_reduce<SumOp, 256>(ss, smem);
+    const float r = 1.0f / sqrtf(ss / (float)cols + eps);
+    const T* src = ADD ? h + row * ldx : xr;
+    for (int64_t c = threadIdx.x; c < cols; c += 256) {
+      float t = Elem<T>::to_f(src[c]) * r;
+      if (CHAIN) t = round_to<T>(t);
+      out[row * ldo + c] = Elem<T>::from_f(Elem<T>::to_f(w[c]) * t);
+    }
+  }
+}
+
+template <typename T, bool CHAIN, bool ADD>
+int launch_rms_norm(const T* x, int64_t ldx, const T* y, T* h, const T* w, T* out,
+                    int64_t ldo, int64_t rows, int64_t cols, float eps,
+                    cudaStream_t stream) {
+  DeviceInfo dev;
+  int st = current_device_info(&dev);
+  if (st != FL_B200_OK) return st;
+  constexpr int VW = Elem<T>::kVec;
+  const bool vec_ok = aligned16(x) && aligned16(w) && aligned16(out) &&
+                      (!ADD || (aligned16(y) && aligned16(h))) && cols % VW == 0 &&
+                      ldx % VW == 0 && ldo % VW == 0;
+  if (vec_ok) {
+    const int64_t nvec = cols / VW;
+    int r = row_ladder(nvec, [&](auto tpr, auto vpt) -> int {
+      constexpr int TPR = decltype(tpr)::value;
+      constexpr int VPT = decltype(vpt)::value;
+      constexpr int BLOCK = ladder_block<TPR>();
+      auto kern = rms_norm_vec_kernel<T, TPR, VPT, BLOCK, CHAIN, ADD>;
+      static const int per_sm = blocks_per_sm(kern, BLOCK, 0);
+      const int64_t units = ceil_div(rows, BLOCK / TPR);
+      const int grid = (int)std::min<int64_t>(units, (int64_t)per_sm * dev.sm_count);
+      kern<<<grid, BLOCK, 0, stream>>>(x, ldx, y, h, w, out, ldo, rows, (int)nvec, eps,
+                                       (float)cols);
+      return launch_status();
+    });
+    if (r >= 0) return r;
+  }
+  auto kern = rms_norm_loop_kernel<T, CHAIN, ADD>;
+  static const int per_sm = blocks_per_sm(kern, 256, 0);
+  const int grid = (int)std::min<int64_t>(rows, (int64_t)per_sm * dev.sm_count);
+  kern<<<grid, 256, 0, stream>>>(x, ldx, y, h, w, out, ldo, rows, cols, eps);
+  return launch_status();
+}
+
+template <bool ADD>
+int rms_norm_entry(const void* x, int64_t ldx, const void* y, void* h, const void* w,
+                   void* out, int64_t ldo, int64_t rows, int64_t cols, float eps,
+                   int dtype, int rounding, cudaStream_t stream) {
+  FLB_CHECK_ARG(rows >= 0 && cols >= 0);
+  if (rows == 0 || cols == 0) return FL_B200_OK;
+  FLB_CHECK_ARG(x && w && out && ldx >= cols && ldo >= cols);
+  FLB_CHECK_ARG(!ADD || (y && h));
+  FLB_CHECK_ARG(rounding == FL_B200_ROUND_FUSED || rounding == FL_B200_ROUND_CHAIN);
+  return dispatch_float(dtype, [&](auto tag) -> int {
+    using T = decltype(tag);
+    auto* xp = static_cast<const T*>(x);
+    auto* yp = static_cast<const T*>(y);
+    auto* hp = static_cast<T*>(h);
+    auto* wp = static_cast<const T*>(w);
+    auto* op = static_cast<T*>(out);
+    if (rounding == FL_B200_ROUND_CHAIN)
+      return launch_rms_norm<T, true, ADD>(xp, ldx, yp, hp, wp, op, ldo, rows, cols, eps,
+                                           stream);
+    return launch_rms_norm<T, false, ADD>(xp, ldx, yp, hp, wp, op, ldo, rows, cols, eps,
+                                          stream);
+  });
+}
+
+}  // namespace
+}  // namespace flb200
+
+extern "C" {
+
+FL_B200_API int fl_b200_rms_norm_fwd(const void* x, int64_t ld_x, const void* w,
+                                     void* out, int64_t ld_out, int64_t rows,
+                                     int64_t cols, float eps, int dtype, int rounding,
+                                     fl_b200_stream_t stream) {
+  return flb200::rms_norm_entry<false>(x, ld_x, nullptr, nullptr, w, out, ld_out, rows,
+                                       cols, eps, dtype, rounding,
+                                       static_cast<cudaStream_t>(stream));
+}
+
+FL_B200_API int fl_b200_add_rms_norm_fwd(const void* x, const void* y, void* h,
+                                         const void* w, void* out, int64_t rows,
+                                         int64_t cols, float eps, int dtype,
+                                         int rounding, fl_b200_stream_t stream) {
+  return flb200::rms_norm_entry<true>(x, cols, y, h, w, out, cols, rows, cols, eps,
+                                      dtype, rounding, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,325 @@
+// RoPE on q/k, and Qwen3's per-head RMSNorm immediately followed by RoPE.
+//
+// Reference behaviour: HF apply_rotary_pos_emb (transformers
+// models/qwen3/modeling_qwen3.py:138-169):
+//   q_embed = q*cos + rotate_half(q)*sin,  rotate_half(x) = cat(-x2, x1)
+// which the reference runs on flagos as neg (csrc/aten/backends/cuda/
+// neg.cu:14-32), cat (cat.cc:13-39), two mul (mul.cu:28-52) and an add
+// (add.cu:48-84) per tensor; and Qwen3's q_norm/k_norm RMSNorm over the
+// head dim right before it (modeling_qwen3.py:248-249,263-268).
+//
+// A head row of D elements is owned by G = D/(2*VW) threads; thread j holds
+// pack j of the low half AND pack j of the high half, so rotate_half needs no
+// data exchange, and the per-head norm needs one G-lane butterfly.
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace flb200 {
+namespace {
+
+struct RopeArgs {
+  const void* q;
+  void* qo;
+  const void* k;
+  void* ko;
+  const void* wq;
+  const void* wk;
+  const void* cos;
+  const void* sin;
+  int64_t sq[3], soq[3], sk[3], sok[3];  // strides over (b, h, s)
+  int64_t scb, scs;                      // cos/sin strides over (b, s)
+  uint32_t Hq, Hk, S, D;
+  float eps;
+};
+
+template <typename T, bool CHAIN>
+__device__ __forceinline__ void rope_pair(float xl, float xh, float cl, float sl,
+                                          float ch, float sh, float& ol, float& oh) {
+  if (CHAIN) {
+    // q*cos -> T;  rotate_half(q)*sin -> T;  sum -> T  (one aten op each)
+    ol = round_to<T>(round_to<T>(xl * cl) + round_to<T>(-xh * sl));
+    oh = round_to<T>(round_to<T>(xh * ch) + round_to<T>(xl * sh));
+  } else {
+    ol = fmaf(xl, cl, -xh * sl);
+    oh = fmaf(xh, ch, xl * sh);
+  }
+}
+
+template <typename T, int G, bool NORM, bool CHAIN>
+__global__ void __launch_bounds__(256) rope_vec_kernel(RopeArgs a, uint32_t units) {
+  constexpr int VW = Elem<T>::kVec;
+  constexpr int UPB = 256 / G;  // head rows per CTA iteration
+  const int j = threadIdx.x % G;
+  const uint32_t htot = a.Hq + a.Hk;
+  const uint32_t half = a.D / 2;
+  for (uint32_t ub = blockIdx.x * UPB; ub < units; ub += gridDim.x * UPB) {
+    const uint32_t u = ub + threadIdx.x / G;
+    const bool valid = u < units;
+    const uint32_t uu = valid ? u : 0;
+    const uint32_t token = uu / htot;
+    const uint32_t head = uu - token * htot;
+    const uint32_t b = token / a.S;
+    const uint32_t s = token - b * a.S;
+    const bool isq = head < a.Hq;
+    const uint32_t hh = isq ? head : head - a.Hq;
+    const T* src;
+    T* dst;
+    const T* w;
+    if (isq) {
+      src = static_cast<const T*>(a.q) + b * a.sq[0] + hh * a.sq[1] + s * a.sq[2];
+      dst = static_cast<T*>(a.qo) + b * a.soq[0] + hh * a.soq[1] + s * a.soq[2];
+      w = static_cast<const T*>(a.wq);
+    } else {
+      src = static_cast<const T*>(a.k) + b * a.sk[0] + hh * a.sk[1] + s * a.sk[2];
+      dst = static_cast<T*>(a.ko) + b * a.sok[0] + hh * a.sok[1] + s * a.sok[2];
+      w = static_cast<const T*>(a.wk);
+    }
+    const uint32_t dl = j * VW;
+    float xl[VW], xh[VW];
+    {
+      uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
+      if (valid) {
+        lo = ld_stream(src + dl);
+        hi = ld_stream(src + half + dl);
+      }
+      unpack<T>(lo, xl);
+      unpack<T>(hi, xh);
+    }
+    if constexpr (NORM) {
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < VW; ++e) ss = fmaf(xl[e], xl[e], fmaf(xh[e], xh[e], ss));
+      ss = group_reduce_warp<SumOp, G>(ss);
+      const float r = 1.0f / sqrtf(ss / (float)a.D + a.eps);
+      if (valid) {
+        float wl[VW], wh[VW];
+        unpack<T>(ld_cached(w + dl), wl);
+        unpack<T>(ld_cached(w + half + dl), wh);
+#pragma unroll
+        for (int e = 0; e < VW; ++e) {
+          if (CHAIN) {
+            xl[e] = round_to<T>(wl[e] * round_to<T>(xl[e] * r));
+            xh[e] = round_to<T>(wh[e] * round_to<T>(xh[e] * r));
+          } else {
+            xl[e] = wl[e] * (xl[e] * r);
+            xh[e] = wh[e] * (xh[e] * r);
+          }
+        }
+      }
+    }
+    if (!valid) continue;
+    const T* cb = static_cast<const T*>(a.cos) + b * a.scb + s * a.scs;
+    const T* sb = static_cast<const T*>(a.sin) + b * a.scb + s * a.scs;
+    float cl[VW], ch[VW], sl[VW], sh[VW];
+    unpack<T>(ld_cached(cb + dl), cl);
+    unpack<T>(ld_cached(cb + half + dl), ch);
+    unpack<T>(ld_cached(sb + dl), sl);
+    unpack<T>(ld_cached(sb + half + dl), sh);
+    float ol[VW], oh[VW];
+#pragma unroll
+    for (int e = 0; e < VW; ++e)
+      rope_pair<T, CHAIN>(xl[e], xh[e], cl[e], sl[e], ch[e], sh[e], ol[e], oh[e]);
+    st_stream(dst + dl, pack<T>(ol));
+    st_stream(dst + half + dl, pack<T>(oh));
+  }
+}
+
+// Any alignment / head dim: one warp per head row, scalar element access.
+template <typename T, bool NORM, bool CHAIN>
+__global__ void __launch_bounds__(256) rope_scalar_kernel(RopeArgs a, uint32_t units) {
+  constexpr int UPB = 256 / 32;
+  const int lane = threadIdx.x & 31;
+  const uint32_t htot = a.Hq + a.Hk;
+  const uint32_t half = a.D / 2;
+  for (uint32_t ub = blockIdx.x * UPB; ub < units; ub += gridDim.x * UPB) {
+    const uint32_t u = ub + threadIdx.x / 32;
+    if (u >= units) continue;  // whole warp leaves together
+    const uint32_t token = u / htot;
+    const uint32_t head = u - token * htot;
+    const uint32_t b = token / a.S;
+    const uint32_t s = token - b * a.S;
+    const bool isq = head < a.Hq;
+    const uint32_t hh = isq ? head : head - a.Hq;
+    const T* src;
+    T* dst;
+    const T* w;
+    if (isq) {
+      src = static_cast<const T*>(a.q) + b * a.sq[0] + hh * a.sq[1] + s * a.sq[2];
+      dst = static_cast<T*>(a.qo) + b * a.soq[0] + hh * a.soq[1] + s * a.soq[2];
+      w = static_cast<const T*>(a.wq);
+    } else {
+      src = static_cast<const T*>(a.k) + b * a.sk[0] + hh * a.sk[1] + s * a.sk[2];
+      dst = static_cast<T*>(a.ko) + b * a.sok[0] + hh * a.sok[1] + s * a.sok[2];
+      w = static_cast<const T*>(a.wk);
+    }
+    float r = 1.f;
+    if constexpr (NORM) {
+      float ss = 0.f;
+      for (uint32_t d = lane; d < a.D; d += 32) {
+        const float v = Elem<T>::to_f(src[d]);
+        ss = fmaf(v, v, ss);
+      }
+      ss = group_reduce_warp<SumOp, 32>(ss);
+      r = 1.0f / sqrtf(ss / (float)a.D + a.eps);
+    }
+    const T* cb = static_cast<const T*>(a.cos) + b * a.scb + s * a.scs;
+    const T* sb = static_cast<const T*>(a.sin) + b * a.scb + s * a.scs;
+    // Read every element this lane needs before writing (in place allowed).
+    for (uint32_t d = lane; d < half; d += 32) {
+      float xl = Elem<T>::to_f(src[d]);
+      float xh = Elem<T>::to_f(src[d + half]);
+      if constexpr (NORM) {
+        const float wl = Elem<T>::to_f(w[d]), wh = Elem<T>::to_f(w[d + half]);
+        if (CHAIN) {
+          xl = round_to<T>(wl * round_to<T>(xl * r));
+          xh = round_to<T>(wh * round_to<T>(xh * r));
+        } else {
+          xl = wl * (xl * r);
+          xh = wh * (xh * r);
+        }
+      }
+      float ol, oh;
+      rope_pair<T, CHAIN>(xl, xh, Elem<T>::to_f(cb[d]), Elem<T>::to_f(sb[d]),
+                          Elem<T>::to_f(cb[d + half]), Elem<T>::to_f(sb[d + half]), ol,
+                          oh);
+      dst[d] = Elem<T>::from_f(ol);
+      dst[d + half] = Elem<T>::from_f(oh);
+    }
+  }
+}
+
+template <typename T, int G, bool NORM, bool CHAIN>
+int launch_vec(const RopeArgs& a, uint32_t units, const DeviceInfo& dev,
+               cudaStream_t stream) {
+  auto kern = rope_vec_kernel<T, G, NORM, CHAIN>;
+  static const int per_sm = blocks_per_sm(kern, 256, 0);
+  const int64_t blocks = ceil_div(units, 256 / G);
+  const int grid = (int)std::min<int64_t>(blocks, (int64_t)per_sm * dev.sm_count);
+  kern<<<grid, 256, 0, stream>>>(a, units);
+  return launch_status();
+}
+
+template <typename T, bool NORM, bool CHAIN>
+int launch_rope(const RopeArgs& a, uint32_t units, cudaStream_t stream) {
+  DeviceInfo dev;
+  int st = current_device_info(&dev);
+  if (st != FL_B200_OK) return st;
+  constexpr int VW = Elem<T>::kVec;
+  const int64_t half = a.D / 2;
+  auto strides_ok = [&](const int64_t* s) {
+    return s[0] % VW == 0 && s[1] % VW == 0 && s[2] % VW == 0;
+  };
+  bool vec_ok = half % VW == 0 && aligned16(a.q) && aligned16(a.qo) &&
+                aligned16(a.cos) && aligned16(a.sin) && strides_ok(a.sq) &&
+                strides_ok(a.soq) && a.scb % VW == 0 && a.scs % VW == 0;
+  if (a.Hk > 0)
+    vec_ok = vec_ok && aligned16(a.k) && aligned16(a.ko) && strides_ok(a.sk) &&
+             strides_ok(a.sok);
+  if (NORM) vec_ok = vec_ok && aligned16(a.wq) && (a.Hk == 0 || aligned16(a.wk));
+  if (vec_ok) {
+    const int64_t g = half / VW;
+    switch (g) {
+      case 1: return launch_vec<T, 1, NORM, CHAIN>(a, units, dev, stream);
+      case 2: return launch_vec<T, 2, NORM, CHAIN>(a, units, dev, stream);
+      case 4: return launch_vec<T, 4, NORM, CHAIN>(a, units, dev, stream);
+      case 8: return launch_vec<T, 8, NORM, CHAIN>(a, units, dev, stream);
+      case 16: return launch_vec<T, 16, NORM, CHAIN>(a, units, dev, stream);
+      case 32: return launch_vec<T, 32, NORM, CHAIN>(a, units, dev, stream);
+      default: break;
+    }
+  }
+  auto kern = rope_scalar_kernel<T, NORM, CHAIN>;
+  static const int per_sm = blocks_per_sm(kern, 256, 0);
+  const int64_t blocks = ceil_div(units, 8);
+  const int grid = (int)std::min<int64_t>(blocks, (int64_t)per_sm * dev.sm_count);
+  kern<<<grid, 256, 0, stream>>>(a, units);
+  return launch_status();
+}
+
+template <bool NORM>
+int rope_entry(RopeArgs& a, int64_t Hq, int64_t Hk, int64_t B, int64_t S, int64_t D,
+               int dtype, int rounding, cudaStream_t stream) {
+  FLB_CHECK_ARG(Hq >= 0 && Hk >= 0 && B >= 0 && S >= 0 && D >= 0);
+  FLB_CHECK_ARG(rounding == FL_B200_ROUND_FUSED || rounding == FL_B200_ROUND_CHAIN);
+  if (a.k == nullptr) Hk = 0;
+  const int64_t units = B * S * (Hq + Hk);
+  if (units == 0 || D == 0) return FL_B200_OK;
+  FLB_CHECK_ARG(D % 2 == 0);
+  FLB_CHECK_ARG(units < (int64_t(1) << 31) && B * S < (int64_t(1) << 31) && D < (1 << 30));
+  FLB_CHECK_ARG(a.cos && a.sin);
+  FLB_CHECK_ARG(Hq == 0 || (a.q && a.qo));
+  FLB_CHECK_ARG(Hk == 0 || (a.k && a.ko));
+  FLB_CHECK_ARG(!NORM || ((Hq == 0 || a.wq) && (Hk == 0 || a.wk)));
+  a.Hq = (uint32_t)Hq;
+  a.Hk = (uint32_t)Hk;
+  a.S = (uint32_t)S;
+  a.D = (uint32_t)D;
+  return dispatch_float(dtype, [&](auto tag) -> int {
+    using T = decltype(tag);
+    if (rounding == FL_B200_ROUND_CHAIN)
+      return launch_rope<T, NORM, true>(a, (uint32_t)units, stream);
+    return launch_rope<T, NORM, false>(a, (uint32_t)units, stream);
+  });
+}
+
+RopeArgs make_args(const void* q, void* q_out, int64_t sqb, int64_t sqh, int64_t sqs,
+                   int64_t soqb, int64_t soqh, int64_t soqs, const void* wq,
+                   const void* k, void* k_out, int64_t skb, int64_t skh, int64_t sks,
+                   int64_t sokb, int64_t sokh, int64_t soks, const void* wk,
+                   const void* cos, const void* sin, int64_t scb, int64_t scs,
+                   float eps) {
+  RopeArgs a{};
+  a.q = q;
+  a.qo = q_out;
+  a.k = k;
+  a.ko = k_out;
+  a.wq = wq;
+  a.wk = wk;
+  a.cos = cos;
+  a.sin = sin;
+  a.sq[0] = sqb, a.sq[1] = sqh, a.sq[2] = sqs;
+  a.soq[0] = soqb, a.soq[1] = soqh, a.soq[2] = soqs;
+  a.sk[0] = skb, a.sk[1] = skh, a.sk[2] = sks;
+  a.sok[0] = sokb, a.sok[1] = sokh, a.sok[2] = soks;
+  a.scb = scb;
+  a.scs = scs;
+  a.eps = eps;
+  return a;
+}
+
+}  // namespace
+}  // namespace flb200
+
+extern "C" {
+
+FL_B200_API int fl_b200_rope_qk(const void* q, void* q_out, int64_t Hq, int64_t sqb,
+                                int64_t sqh, int64_t sqs, int64_t soqb, int64_t soqh,
+                                int64_t soqs, const void* k, void* k_out, int64_t Hk,
+                                int64_t skb, int64_t skh, int64_t sks, int64_t sokb,
+                                int64_t sokh, int64_t soks, const void* cos,
+                                const void* sin, int64_t scb, int64_t scs, int64_t B,
+                                int64_t S, int64_t D, int dtype, int rounding,
+                                fl_b200_stream_t stream) {
+  auto a = flb200::make_args(q, q_out, sqb, sqh, sqs, soqb, soqh, soqs, nullptr, k,
+                             k_out, skb, skh, sks, sokb, sokh, soks, nullptr, cos, sin,
+                             scb, scs, 0.f);
+  return flb200::rope_entry<false>(a, Hq, Hk, B, S, D, dtype, rounding,
+                                   static_cast<cudaStream_t>(stream));
+}
+
+FL_B200_API int fl_b200_rms_norm_rope(
+    const void* q, void* q_out, int64_t Hq, int64_t sqb, int64_t sqh, int64_t sqs,
+    int64_t soqb, int64_t soqh, int64_t soqs, const void* wq, const void* k,
+    void* k_out, int64_t Hk, int64_t skb, int64_t skh, int64_t sks, int64_t sokb,
+    int64_t sokh, int64_t soks, const void* wk, const void* cos, const void* sin,
+    int64_t scb, int64_t scs, int64_t B, int64_t S, int64_t D, float eps, int dtype,
+    int rounding, fl_b200_stream_t stream) {
+  auto a = flb200::make_args(q, q_out, sqb, sqh, sqs, soqb, soqh, soqs, wq, k, k_out,
+                             skb, skh, sks, sokb, sokh, soks, wk, cos, sin, scb, scs,
+                             eps);
+  return flb200::rope_entry<true>(a, Hq, Hk, B, S, D, dtype, rounding,
+                                  static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

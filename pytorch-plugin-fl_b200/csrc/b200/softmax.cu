@@ -1,0 +1,291 @@
+// Softmax with fp32 accumulation; last-dim (optionally causal) and middle-dim.
+//
+// Reference behaviour: _softmax(self, dim, half_to_float) (register.cc:
+// 270-272 -> csrc/aten/backends/cuda/softmax.cc:14-40, PyTorch's host_softmax)
+// on logits that HF has already masked (modeling_qwen3.py:209-213).  The
+// causal variant applies the mask itself: masked keys are never read and are
+// written as exact zeros, so a causal row of L keys costs (i+1)/L of a read.
+//
+// exp(x - m) is evaluated as exp2f(x*log2e - m*log2e) with one FMA; the row
+// stays in registers (row_ladder), so HBM sees one read and one write.
+#include "row_ladder.cuh"
+
+namespace flb200 {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float exp_shifted(float x, float mlog2e) {
+  return exp2f(fmaf(x, kLog2e, -mlog2e));
+}
+
+// Stores VW fp32 values (one input pack's worth) as TO at `o`.
+template <typename TO, int VW>
+__device__ __forceinline__ void store_vals(TO* o, const float (&v)[VW]) {
+  constexpr int OW = Elem<TO>::kVec;
+  static_assert(VW % OW == 0, "input pack must cover whole output packs");
+#pragma unroll
+  for (int c = 0; c < VW / OW; ++c) {
+    float t[OW];
+#pragma unroll
+    for (int e = 0; e < OW; ++e) t[e] = v[c * OW + e];
+    st_stream(o + c * OW, pack<TO>(t));
+  }
+}
+
+// Sets elements [keep, VW) of a pack to -inf (the masked tail of a causal row).
+template <typename T>
+__device__ __forceinline__ uint4 mask_tail(uint4 v, int keep);
+template <>
+__device__ __forceinline__ uint4 mask_tail<float>(uint4 v, int keep) {
+  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    if (e >= keep) w[e] = 0xff800000u;
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+template <uint16_t NEG_INF>
+__device__ __forceinline__ uint4 mask_tail16(uint4 v, int keep) {
+  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (2 * i >= keep) w[i] = (w[i] & 0xffff0000u) | NEG_INF;
+    if (2 * i + 1 >= keep) w[i] = (w[i] & 0x0000ffffu) | ((uint32_t)NEG_INF << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+template <>
+__device__ __forceinline__ uint4 mask_tail<__nv_bfloat16>(uint4 v, int keep) {
+  return mask_tail16<0xff80>(v, keep);
+}
+template <>
+__device__ __forceinline__ uint4 mask_tail<__half>(uint4 v, int keep) {
+  return mask_tail16<0xfc00>(v, keep);
+}
+
+// Masked keys are loaded as -inf, so the max ignores them, their exp is an
+// exact 0 and a row with no visible key comes out NaN (-inf - -inf), with no
+// per-element masks in the arithmetic.
+template <typename TI, typename TO, int TPR, int VPT, int BLOCK, bool CAUSAL>
+__global__ void __launch_bounds__(BLOCK, ladder_min_blocks<BLOCK>())
+softmax_vec_kernel(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
+                   int64_t cols, int64_t q_len, int64_t offset) {
+  constexpr int VW = Elem<TI>::kVec;
+  constexpr int RPB = BLOCK / TPR;
+  __shared__ float smem[BLOCK / 32];
+  const int slot = threadIdx.x / TPR;
+  const int lane = threadIdx.x % TPR;
+  const int nvec = (int)(cols / VW);
+  for (int64_t base = (int64_t)blockIdx.x * RPB; base < rows;
+       base += (int64_t)gridDim.x * RPB) {
+    const int64_t row = base + slot;
+    const bool ok = row < rows;
+    // Visible keys of this row, clamped to [0, cols].
+    int nvalid = (int)cols;
+    if (CAUSAL) nvalid = (int)max((int64_t)0, min(cols, (row % q_len) + offset + 1));
+    const TI* xr = x + row * ldx;
+    uint4 v[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int j0 = (lane + i * TPR) * VW;
+      if (ok && j0 < nvalid) {
+        v[i] = ld_stream(xr + j0);
+        if (CAUSAL && j0 + VW > nvalid) v[i] = mask_tail<TI>(v[i], nvalid - j0);
+      } else {
+        v[i] = mask_tail<TI>(make_uint4(0, 0, 0, 0), 0);
+      }
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      float f[VW];
+      unpack<TI>(v[i], f);
+#pragma unroll
+      for (int e = 0; e < VW; ++e) m = fmaxf(m, f[e]);
+    }
+    m = row_reduce<FastMaxOp, TPR, BLOCK>(m, smem);
+    const float ml = m * kLog2e;
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      float f[VW];
+      unpack<TI>(opaque(v[i]), f);
+#pragma unroll
+      for (int e = 0; e < VW; ++e) s += exp_shifted(f[e], ml);
+    }
+    s = row_reduce<SumOp, TPR, BLOCK>(s, smem);
+    const float inv = 1.0f / s;
+    TO* yr = y + row * ldy;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = lane + i * TPR;
+      if (!ok || vi >= nvec) continue;
+      float f[VW], o[VW];
+      unpack<TI>(opaque(v[i]), f);
+#pragma unroll
+      for (int e = 0; e < VW; ++e) o[e] = exp_shifted(f[e], ml) * inv;
+      store_vals<TO, VW>(yr + (int64_t)vi * VW, o);
+    }
+  }
+}
+
+// Any row length / alignment: one CTA per row; per-thread online max/sum,
+// then a CTA combine; the row is read twice (the second read mostly from L2).
+template <typename TI, typename TO, bool CAUSAL>
+__global__ void __launch_bounds__(256)
+softmax_loop_kernel(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
+                    int64_t cols, int64_t q_len, int64_t offset) {
+  __shared__ float smem[256 / 32];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    int64_t nvalid = cols;
+    if (CAUSAL) nvalid = min(cols, (row % q_len) + offset + 1);
+    const TI* xr = x + row * ldx;
+    float m = -INFINITY, s = 0.f;
+    for (int64_t c = threadIdx.x; c < nvalid; c += 256) {
+      const float f = Elem<TI>::to_f(xr[c]);
+      if (f > m) {
+        s = s * exp2f((m - f) * kLog2e) + 1.0f;  // rescale the running sum
+        m = f;
+      } else if (f != -INFINITY) {  // exp(-inf) adds nothing (and -inf - -inf is NaN)
+        s += exp2f((f - m) * kLog2e);
+      }
+    }
+    const float mrow = block_reduce<FastMaxOp, 256>(m, smem);
+    // Rescale each thread's partial sum to the row max (empty partials add 0).
+    const float part = (m == -INFINITY) ? 0.f : s * exp2f((m - mrow) * kLog2e);
+    const float srow = block_reduce<SumOp, 256>(part, smem);
+    const float inv = nvalid > 0 ? 1.0f / srow : __int_as_float(0x7fc00000);
+    const float ml = mrow * kLog2e;
+    TO* yr = y + row * ldy;
+    for (int64_t c = threadIdx.x; c < cols; c += 256) {
+      float o;
+      if (c < nvalid) o = exp_shifted(Elem<TI>::to_f(xr[c]), ml) * inv;
+      else o = nvalid > 0 ? 0.f : inv;
+      if constexpr (std::is_same<TO, float>::value) yr[c] = o;
+      else yr[c] = Elem<TO>::from_f(o);
+    }
+  }
+}
+
+// Softmax over the middle dim of a dense [outer, n, inner] view: one thread
+// per (outer, inner) column, three passes over n (coalesced across inner).
+template <typename TI, typename TO>
+__global__ void __launch_bounds__(256)
+softmax_middim_kernel(const TI* x, TO* y, int64_t outer, int64_t n, int64_t inner) {
+  const int64_t cols = outer * inner;
+  for (int64_t t = (int64_t)blockIdx.x * 256 + threadIdx.x; t < cols;
+       t += (int64_t)gridDim.x * 256) {
+    const int64_t o = t / inner, in = t - o * inner;
+    const TI* xc = x + o * n * inner + in;
+    TO* yc = y + o * n * inner + in;
+    float m = -INFINITY;
+    for (int64_t k = 0; k < n; ++k) m = fmaxf(m, Elem<TI>::to_f(xc[k * inner]));
+    const float ml = m * kLog2e;
+    float s = 0.f;
+    for (int64_t k = 0; k < n; ++k) s += exp_shifted(Elem<TI>::to_f(xc[k * inner]), ml);
+    const float inv = 1.0f / s;
+    for (int64_t k = 0; k < n; ++k) {
+      const float v = exp_shifted(Elem<TI>::to_f(xc[k * inner]), ml) * inv;
+      if constexpr (std::is_same<TO, float>::value) yc[k * inner] = v;
+      else yc[k * inner] = Elem<TO>::from_f(v);
+    }
+  }
+}
+
+template <typename TI, typename TO, bool CAUSAL>
+int launch_softmax(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
+                   int64_t cols, int64_t q_len, int64_t offset, cudaStream_t stream) {
+  DeviceInfo dev;
+  int st = current_device_info(&dev);
+  if (st != FL_B200_OK) return st;
+  constexpr int VW = Elem<TI>::kVec;
+  const bool vec_ok = aligned16(x) && aligned16(y) && cols % VW == 0 && ldx % VW == 0 &&
+                      ldy % VW == 0;
+  if (vec_ok) {
+    int r = row_ladder<8>(cols / VW, [&](auto tpr, auto vpt) -> int {
+      constexpr int TPR = decltype(tpr)::value;
+      constexpr int VPT = decltype(vpt)::value;
+      constexpr int BLOCK = ladder_block<TPR>();
+      auto kern = softmax_vec_kernel<TI, TO, TPR, VPT, BLOCK, CAUSAL>;
+      static const int per_sm = blocks_per_sm(kern, BLOCK, 0);
+      const int64_t units = ceil_div(rows, BLOCK / TPR);
+      const int grid = (int)std::min<int64_t>(units, (int64_t)per_sm * dev.sm_count);
+      kern<<<grid, BLOCK, 0, stream>>>(x, ldx, y, ldy, rows, cols, q_len, offset);
+      return launch_status();
+    });
+    if (r >= 0) return r;
+  }
+  auto kern = softmax_loop_kernel<TI, TO, CAUSAL>;
+  static const int per_sm = blocks_per_sm(kern, 256, 0);
+  const int grid = (int)std::min<int64_t>(rows, (int64_t)per_sm * dev.sm_count);
+  kern<<<grid, 256, 0, stream>>>(x, ldx, y, ldy, rows, cols, q_len, offset);
+  return launch_status();
+}
+
+// Calls f(TI{}, TO{}) for the supported (in, out) pairs: out == in, or
+// 16-bit in with fp32 out (half_to_float).
+template <typename F>
+int dispatch_in_out(int in_dtype, int out_dtype, F&& f) {
+  if (in_dtype == out_dtype) {
+    return dispatch_float(in_dtype, [&](auto t) { return f(t, t); });
+  }
+  if (out_dtype == FL_B200_F32) {
+    if (in_dtype == FL_B200_BF16) return f(__nv_bfloat16{}, float{});
+    if (in_dtype == FL_B200_F16) return f(__half{}, float{});
+  }
+  return FL_B200_ERR_UNSUPPORTED_DTYPE;
+}
+
+}  // namespace
+}  // namespace flb200
+
+extern "C" {
+
+FL_B200_API int fl_b200_softmax_lastdim(const void* x, int64_t ld_x, void* out,
+                                        int64_t ld_out, int64_t rows, int64_t cols,
+                                        int in_dtype, int out_dtype, int causal,
+                                        int64_t q_len, int64_t causal_offset,
+                                        fl_b200_stream_t stream) {
+  using namespace flb200;
+  FLB_CHECK_ARG(rows >= 0 && cols >= 0);
+  if (rows == 0 || cols == 0) return FL_B200_OK;
+  FLB_CHECK_ARG(x && out && ld_x >= cols && ld_out >= cols);
+  if (causal) FLB_CHECK_ARG(q_len > 0);
+  auto s = static_cast<cudaStream_t>(stream);
+  return dispatch_in_out(in_dtype, out_dtype, [&](auto ti, auto to) -> int {
+    using TI = decltype(ti);
+    using TO = decltype(to);
+    auto xp = static_cast<const TI*>(x);
+    auto yp = static_cast<TO*>(out);
+    if (causal)
+      return launch_softmax<TI, TO, true>(xp, ld_x, yp, ld_out, rows, cols, q_len,
+                                          causal_offset, s);
+    return launch_softmax<TI, TO, false>(xp, ld_x, yp, ld_out, rows, cols, 1, 0, s);
+  });
+}
+
+FL_B200_API int fl_b200_softmax_middim(const void* x, void* out, int64_t outer,
+                                       int64_t n, int64_t inner, int in_dtype,
+                                       int out_dtype, fl_b200_stream_t stream) {
+  using namespace flb200;
+  FLB_CHECK_ARG(outer >= 0 && n >= 0 && inner >= 0);
+  if (outer == 0 || n == 0 || inner == 0) return FL_B200_OK;
+  FLB_CHECK_ARG(x && out);
+  DeviceInfo dev;
+  int st = current_device_info(&dev);
+  if (st != FL_B200_OK) return st;
+  auto s = static_cast<cudaStream_t>(stream);
+  return dispatch_in_out(in_dtype, out_dtype, [&](auto ti, auto to) -> int {
+    using TI = decltype(ti);
+    using TO = decltype(to);
+    auto kern = softmax_middim_kernel<TI, TO>;
+    const int per_sm = blocks_per_sm(kern, 256, 0);
+    const int grid = (int)std::max<int64_t>(
+        1, std::min<int64_t>(ceil_div(outer * inner, 256), (int64_t)per_sm * dev.sm_count));
+    kern<<<grid, 256, 0, s>>>(static_cast<const TI*>(x), static_cast<TO*>(out), outer, n,
+                              inner);
+    return launch_status();
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,217 @@
+"""Generate tests/golden/golden.npz: golden vectors of the reference's own path.
+
+The reference computes RMSNorm, RoPE and SwiGLU as the HuggingFace formulas
+(transformers models/qwen3/modeling_qwen3.py) over aten ops, and softmax /
+sum / mean / amax / argmax / add / mul as aten ops.  This script runs exactly
+that on torch CPU (PyTorch 2.11, the version the reference pins), using the
+transformers 5.5.0 modules themselves where they exist (Qwen3RMSNorm,
+Qwen3RotaryEmbedding, apply_rotary_pos_emb, ACT2FN["silu"]), on seeded
+inputs with the distributions of the benchmark configs, and stores inputs and
+outputs.  It also checks that oracle/hf_chain.py (the restated formulas used
+as the CPU baseline) reproduces the transformers modules bit for bit.
+
+Run from the repository root:  python tests/golden/make_golden.py
+bf16 arrays are stored as uint16 bit patterns under keys ending in ':bf16'.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+from oracle import hf_chain  # noqa: E402
+
+OUT = os.path.join(HERE, "golden.npz")
+
+
+def _store(d: dict, key: str, t: torch.Tensor) -> None:
+    t = t.detach().cpu()
+    if t.dtype == torch.bfloat16:
+        d[key + ":bf16"] = t.view(torch.int16).numpy().view(np.uint16)
+    elif t.dtype == torch.float16:
+        d[key + ":f16"] = t.numpy()
+    elif t.dtype == torch.float32:
+        d[key + ":f32"] = t.numpy()
+    elif t.dtype in (torch.int32, torch.int64):
+        d[key + ":int"] = t.numpy()
+    else:
+        raise TypeError(t.dtype)
+
+
+def _gen(seed: int) -> torch.Generator:
+    return torch.Generator().manual_seed(seed)
+
+
+def main() -> None:
+    from transformers.activations import ACT2FN
+    from transformers.models.qwen3 import modeling_qwen3 as mq
+    from transformers.models.qwen3.configuration_qwen3 import Qwen3Config
+
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    d: dict[str, np.ndarray] = {}
+
+    # --- RMSNorm, fp32, the CPU-oracle config's distribution (eps 1e-6, seed 0)
+    g = _gen(0)
+    x = torch.randn(16, 4096, generator=g)
+    w = 1 + 0.1 * torch.randn(4096, generator=g)
+    mod = mq.Qwen3RMSNorm(4096, eps=1e-6)
+    with torch.no_grad():
+        mod.weight.copy_(w)
+        y = mod(x)
+    assert torch.equal(y, hf_chain.rms_norm(x, w, 1e-6))
+    _store(d, "rmsnorm_f32/x", x)
+    _store(d, "rmsnorm_f32/w", w)
+    _store(d, "rmsnorm_f32/out", y)
+
+    # --- RMSNorm, bf16, the decoder-chain config (eps 1e-5)
+    g = _gen(1)
+    x = torch.randn(16, 4096, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(4096, generator=g)).to(torch.bfloat16)
+    mod = mq.Qwen3RMSNorm(4096, eps=1e-5).to(torch.bfloat16)
+    with torch.no_grad():
+        mod.weight.copy_(w)
+        y = mod(x)
+    assert torch.equal(y, hf_chain.rms_norm(x, w, 1e-5))
+    _store(d, "rmsnorm_bf16/x", x)
+    _store(d, "rmsnorm_bf16/w", w)
+    _store(d, "rmsnorm_bf16/out", y)
+
+    # --- RoPE tables + apply, bf16, theta 1e4, head dim 128; positions cover
+    # the start and the end of the 8192-token config.
+    cfg = Qwen3Config(head_dim=128, hidden_size=4096, num_attention_heads=32,
+                      num_key_value_heads=8, max_position_embeddings=8192,
+                      rope_parameters={"rope_type": "default", "rope_theta": 10000.0})
+    rot = mq.Qwen3RotaryEmbedding(cfg)
+    pos = torch.tensor([list(range(0, 8)) + list(range(8184, 8192))], dtype=torch.int64)
+    S = pos.shape[1]
+    g = _gen(2)
+    q = torch.randn(1, S, 32, 128, generator=g).to(torch.bfloat16).transpose(1, 2)
+    k = torch.randn(1, S, 8, 128, generator=g).to(torch.bfloat16).transpose(1, 2)
+    with torch.no_grad():
+        cos, sin = rot(q, pos)
+    c2, s2 = hf_chain.rope_tables(pos, 128, 10000.0, torch.bfloat16)
+    assert torch.equal(cos, c2) and torch.equal(sin, s2)
+    qe, ke = mq.apply_rotary_pos_emb(q, k, cos, sin)
+    qe2, ke2 = hf_chain.rope(q, k, cos, sin)
+    assert torch.equal(qe, qe2) and torch.equal(ke, ke2)
+    _store(d, "rope_bf16/pos", pos)
+    _store(d, "rope_bf16/q", q.contiguous())       # [B, H, S, D]
+    _store(d, "rope_bf16/k", k.contiguous())
+    _store(d, "rope_bf16/cos", cos)                # [B, S, D]
+    _store(d, "rope_bf16/sin", sin)
+    _store(d, "rope_bf16/q_out", qe.contiguous())
+    _store(d, "rope_bf16/k_out", ke.contiguous())
+
+    # --- Qwen3 q_norm / k_norm (RMSNorm over the head dim, eps 1e-6) then RoPE
+    wq = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16)
+    wk = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16)
+    qn_mod = mq.Qwen3RMSNorm(128, eps=1e-6).to(torch.bfloat16)
+    kn_mod = mq.Qwen3RMSNorm(128, eps=1e-6).to(torch.bfloat16)
+    with torch.no_grad():
+        qn_mod.weight.copy_(wq)
+        kn_mod.weight.copy_(wk)
+        qn = qn_mod(q)
+        kn = kn_mod(k)
+    qe, ke = mq.apply_rotary_pos_emb(qn, kn, cos, sin)
+    _store(d, "qknorm_rope_bf16/wq", wq)
+    _store(d, "qknorm_rope_bf16/wk", wk)
+    _store(d, "qknorm_rope_bf16/q_out", qe.contiguous())
+    _store(d, "qknorm_rope_bf16/k_out", ke.contiguous())
+
+    # --- SwiGLU, bf16 (act_fn = silu)
+    g = _gen(3)
+    gate = torch.randn(16, 1024, generator=g).to(torch.bfloat16)
+    up = torch.randn(16, 1024, generator=g).to(torch.bfloat16)
+    a = ACT2FN["silu"](gate) * up
+    assert torch.equal(a, hf_chain.swiglu(gate, up))
+    _store(d, "swiglu_bf16/gate", gate)
+    _store(d, "swiglu_bf16/up", up)
+    _store(d, "swiglu_bf16/out", a)
+
+    # --- causal softmax, bf16 logits ~ N(0, 3^2), upper triangle -inf
+    g = _gen(4)
+    L = 64
+    logits = (3.0 * torch.randn(2, 4, L, L, generator=g)).to(torch.bfloat16)
+    mask = torch.triu(torch.ones(L, L, dtype=torch.bool), diagonal=1)
+    logits = logits.masked_fill(mask, float("-inf"))
+    p32 = torch.softmax(logits, dim=-1, dtype=torch.float32)   # HF eager attention
+    p16 = torch.softmax(logits, dim=-1)                        # _softmax, bf16 out
+    _store(d, "softmax_causal_bf16/x", logits)
+    _store(d, "softmax_causal_bf16/out_f32", p32)
+    _store(d, "softmax_causal_bf16/out_bf16", p16)
+
+    # --- softmax, fp16 and fp32 (the reference's own test shapes)
+    g = _gen(5)
+    x16 = torch.randn(4, 8, 128, generator=g).to(torch.float16)
+    _store(d, "softmax_f16/x", x16)
+    _store(d, "softmax_f16/out", torch.softmax(x16, dim=-1))
+    x32 = torch.randn(16, 32, generator=g)
+    _store(d, "softmax_f32/x", x32)
+    _store(d, "softmax_f32/out", torch.softmax(x32, dim=-1))
+    _store(d, "softmax_f32/out_dim0", torch.softmax(x32, dim=0))
+
+    # --- reductions, fp32 ~ N(0,1)
+    g = _gen(6)
+    xr = torch.randn(16, 8192, generator=g)
+    _store(d, "reduce_f32/x", xr)
+    _store(d, "reduce_f32/sum_last", xr.sum(-1))
+    _store(d, "reduce_f32/mean_last", xr.mean(-1))
+    _store(d, "reduce_f32/amax_last", xr.amax(-1))
+    _store(d, "reduce_f32/sum_all", xr.sum())
+    _store(d, "reduce_f32/mean_all", xr.mean())
+    _store(d, "reduce_f32/amax_all", xr.amax())
+    _store(d, "reduce_f32/sum_dim0", xr.sum(0))
+
+    # --- argmax, bf16 ~ N(0,1) [8, 32000], with planted ties and NaNs
+    g = _gen(7)
+    xa = torch.randn(8, 32000, generator=g).to(torch.bfloat16)
+    xa[3, 100] = 9.0
+    xa[3, 31999] = 9.0                   # tie: the first index wins
+    xa[5, 7] = float("nan")
+    xa[5, 20000] = float("nan")          # first NaN wins
+    xa[6, :] = float("-inf")             # all -inf: index 0
+    _store(d, "argmax_bf16/x", xa)
+    _store(d, "argmax_bf16/out", xa.argmax(-1))
+
+    # --- int32 -> int64 sums, U[-1000, 1000]
+    g = _gen(8)
+    xi = torch.randint(-1000, 1001, (16, 8192), generator=g, dtype=torch.int32)
+    _store(d, "sum_i32/x", xi)
+    _store(d, "sum_i32/sum_last", xi.sum(-1))
+    _store(d, "sum_i32/sum_all", xi.sum())
+
+    # --- broadcast add / mul (the reference's own test shapes + the chain's)
+    g = _gen(9)
+    a = torch.randn(4, 8, generator=g).to(torch.bfloat16)
+    b = torch.randn(8, generator=g).to(torch.bfloat16)
+    _store(d, "add_bf16/a", a)
+    _store(d, "add_bf16/b", b)
+    _store(d, "add_bf16/out", a + b)
+    _store(d, "add_bf16/out_alpha", torch.add(a, b, alpha=2.5))
+    xr_ = torch.randn(16, 4096, generator=g).to(torch.bfloat16)
+    yr_ = torch.randn(16, 4096, generator=g).to(torch.bfloat16)
+    _store(d, "residual_bf16/x", xr_)
+    _store(d, "residual_bf16/y", yr_)
+    _store(d, "residual_bf16/out", xr_ + yr_)
+    wv = (1 + 0.1 * torch.randn(512, generator=g)).to(torch.bfloat16)
+    hv = torch.randn(8, 512, generator=g).to(torch.bfloat16)
+    cv = torch.randn(8, 1, generator=g).to(torch.bfloat16)
+    _store(d, "mul_bf16/w", wv)
+    _store(d, "mul_bf16/h", hv)
+    _store(d, "mul_bf16/c", cv)
+    _store(d, "mul_bf16/w_h", wv * hv)
+    _store(d, "mul_bf16/h_c", hv * cv)
+
+    np.savez_compressed(OUT, **d)
+    print(f"wrote {OUT}: {len(d)} arrays, {os.path.getsize(OUT)} bytes")
+
+
+if __name__ == "__main__":
+    main()

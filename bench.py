@@ -503,7 +503,8 @@ def correctness_sample(stack, K, world, rank, dev):
     stack._rope()
     a, h = K.swiglu_residual(stack.g, stack.u, stack.x0, stack.y, rounding=stack.rounding)
     parts = [stack.x0[rows], stack.y[rows], n[rows], stack.g[rows], stack.u[rows], a[rows], h[rows],
-             stack.q[0, rows].reshape(4, -1), stack.qo[0, rows].reshape(4, -1)]
+             stack.q[0, rows].reshape(4, -1), stack.qo[0, rows].reshape(4, -1),
+             stack.cos[rows], stack.sin[rows]]
     flat = torch.cat([p.reshape(-1) for p in parts])
     if world > 1:
         import torch.distributed as dist
@@ -520,13 +521,17 @@ def correctness_sample(stack, K, world, rank, dev):
     from oracle import ops
 
     worst = 0
+    table_ulp = 0
     sizes = [p.numel() for p in parts]
     w0 = stack.w[0].float().cpu().numpy()
     for r in range(world):
         vals = torch.split(gathered[r].float().cpu(), sizes)
-        x, y, nn, g, u, a_, h_, q, qo = [v.numpy().reshape(4, -1) for v in vals]
+        x, y, nn, g, u, a_, h_, q, qo, ct, st = [v.numpy().reshape(4, -1) for v in vals]
+        # the rows' cos/sin are the rank's global positions r*T + {0, 1, T/2, T-1}
         pos = r * stack.T + np.array([0, 1, stack.T // 2, stack.T - 1])
-        ct, st = ops.rope_tables(pos, HEAD, THETA, "bf16")
+        ct_o, st_o = ops.rope_tables(pos, HEAD, THETA, "bf16")
+        table_ulp = max(table_ulp, int(max(ops.ulp_diff(ct, ct_o, "bf16").max(),
+                                           ops.ulp_diff(st, st_o, "bf16").max())))
         checks = [
             (nn, ops.rms_norm_golden(x, w0, EPS, "bf16") if stack.rounding == "fused"
              else ops.rms_norm_chain(x, w0, EPS, "bf16")),
@@ -539,7 +544,8 @@ def correctness_sample(stack, K, world, rank, dev):
         checks.append((qo, qref))
         for got, ref in checks:
             worst = max(worst, int(ops.ulp_diff(got, ref, "bf16").max()))
-    return {"max_ulp_vs_oracle": worst, "ranks_checked": world, "ok": worst <= 1}
+    return {"max_ulp_vs_oracle": worst, "ranks_checked": world, "ok": worst <= 1,
+            "rope_table_max_ulp_vs_oracle_tables": table_ulp}
 
 
 if __name__ == "__main__":

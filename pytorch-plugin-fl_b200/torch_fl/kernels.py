@@ -68,7 +68,9 @@ def _rows_view(x: torch.Tensor) -> tuple[int, int, int]:
     if x.dim() == 0:
         return 1, 1, 1
     cols = x.shape[-1]
-    rows = x.numel() // cols if cols else 0
+    rows = 1
+    for s in x.shape[:-1]:
+        rows *= s
     if x.stride(-1) != 1 and cols > 1:
         raise ValueError("last dim must be contiguous")
     if x.dim() == 1 or rows <= 1:

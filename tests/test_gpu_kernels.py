@@ -51,8 +51,10 @@ def test_rms_norm_chain_matches_reference_chain(dtype):
     out = K.rms_norm(x, w, 1e-5, rounding="chain")
     dt = parity.dname(dtype)
     ref = ops.rms_norm_chain(parity.to_np(x), parity.to_np(w), 1e-5, dt)
-    d = parity.assert_ulp(parity.to_np(out), ref, dt, 1, "chain")
-    assert np.mean(d == 0) > 0.999  # differs only where fp32 sum order flips a rounding
+    # Differs only where the fp32 sum order flips the intermediate rounding of
+    # x*r; the weight multiply can carry that 1-ulp flip into a 2-ulp one.
+    d = parity.assert_ulp(parity.to_np(out), ref, dt, 2, "chain")
+    assert np.mean(d == 0) > 0.999
 
 
 def test_rms_norm_golden_fixtures(golden):
@@ -213,8 +215,10 @@ def test_swiglu(dtype, shape):
     dt = parity.dname(dtype)
     check_float(K.swiglu(g, u), ops.swiglu_golden(parity.to_np(g), parity.to_np(u), dt), dt, "fused")
     if dt != "f32":
+        # CUDA's expf and the host's differ in the last fp32 bit; where that
+        # flips the rounding of silu, the multiply by `up` can make it 2 ulp.
         d = parity.assert_ulp(parity.to_np(K.swiglu(g, u, rounding="chain")),
-                              ops.swiglu_chain(parity.to_np(g), parity.to_np(u), dt), dt, 1, "chain")
+                              ops.swiglu_chain(parity.to_np(g), parity.to_np(u), dt), dt, 2, "chain")
         assert np.mean(d == 0) > 0.999
 
 
@@ -318,10 +322,15 @@ def test_binary_scalar_keeps_opmath():
 def test_cast_all_pairs():
     vals = torch.tensor([0.0, -0.0, 1.0, -2.5, 65504.0, 1e-8, 3.14159, -1000.75, 7.0, 2**24 + 1.0])
     for s in [torch.float32, torch.bfloat16, torch.float16, torch.int32, torch.int64]:
-        src = vals.to(s) if not s.is_floating_point else vals.to(s)
+        src = vals.to(s)
         for d in [torch.float32, torch.bfloat16, torch.float16, torch.int32, torch.int64]:
             got = K.cast(src.to(DEV), d).cpu()
             ref = src.to(d)    # torch CPU cast semantics
+            if s.is_floating_point and not d.is_floating_point:
+                # float -> int of inf / out-of-range values is unspecified (C
+                # semantics; x86 and the GPU saturate differently): skip those
+                ok = torch.isfinite(src.float())
+                got, ref = got[ok], ref[ok]
             assert torch.equal(got, ref), (s, d, got, ref)
     x = rnd((1 << 20,), torch.float32, 31)
     assert torch.equal(K.cast(x, torch.bfloat16).cpu(), x.cpu().to(torch.bfloat16))

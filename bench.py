@@ -408,7 +408,8 @@ def main():
         b = bytes_of[name] * T
         per_op[name] = {"ms": round(m, 4), "gbs": round(b / (m * 1e-3) / 1e9, 1),
                         "launches": counts[name]}
-    dom = "swiglu_residual" if "swiglu_residual" in kern_ms else "swiglu"
+    # the dominant kernel: the largest total device time inside the timed region
+    dom = max(kern_ms, key=lambda k: kern_ms[k] * counts[k])
     dom_bytes = bytes_of[dom] * T
     achieved = dom_bytes / (kern_ms[dom] * 1e-3) / 1e9
     peak, peak_kind = measured_peak()

@@ -257,6 +257,31 @@ FL_B200_API int fl_b200_sum_i32_i64(const int32_t* x, int64_t ld, int64_t rows,
                                     void* workspace, size_t workspace_bytes,
                                     fl_b200_stream_t stream);
 
+/* ------------------------------------------------------------------------ *
+ * Full-tensor sum that allocates nothing.  No counterpart in the reference: *
+ * it exists for callers that cannot allocate device memory themselves --   *
+ * code bound through a C FFI that only receives tensors from its host      *
+ * framework and has no handle on that framework's allocator, or code that  *
+ * runs where a cudaMalloc would synchronise the device or is not allowed.  *
+ * Same result as fl_b200_reduce_sum_all (same kernel and split), but the   *
+ * cross-CTA partials live in a fixed scratch array of                      *
+ * FL_B200_NOALLOC_SCRATCH_BYTES inside this library: every GPU that loads  *
+ * the library holds that array until the process exits.  A full-tensor    *
+ * sum splits into at most 2048 partials (32 KiB); a request whose split    *
+ * would not fit the scratch is rejected with FL_B200_ERR_TOO_LARGE before  *
+ * anything is launched.                                                    *
+ * The first call on a device looks up the scratch's device address        *
+ * (cudaGetSymbolAddress) and caches it; make that first call before any    *
+ * stream capture.  Every call shares the one scratch array, which keeps    *
+ * the previous call's contents (the call zeroes what must start at zero):  *
+ * calls that can overlap on the GPU -- on different streams, or from       *
+ * different host threads -- race on it and must be serialised by the      *
+ * caller.                                                                  */
+#define FL_B200_NOALLOC_SCRATCH_BYTES 65536
+FL_B200_API int fl_b200_reduce_sum_all_noalloc(const void* x, int64_t n, void* out,
+                                               int in_dtype, int out_dtype,
+                                               fl_b200_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -15,6 +15,9 @@
 // partials in chunk order, so the result does not depend on CTA timing.
 #include "common.cuh"
 
+#include <atomic>
+#include <mutex>
+
 namespace flb200 {
 namespace {
 
@@ -512,3 +515,69 @@ FL_B200_API int fl_b200_sum_i32_i64(const int32_t* x, int64_t ld, int64_t rows,
 }
 
 }  // extern "C"
+
+// ---- full-tensor sum without any allocation ---------------------------------
+// The partials of fl_b200_reduce_sum_all_noalloc live here.  In host code the
+// name g_noalloc_scratch is only a host-side stand-in for the symbol, never a
+// device address: the device address is looked up per device with
+// cudaGetSymbolAddress and passed to the kernel like a caller's workspace.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[FL_B200_NOALLOC_SCRATCH_BYTES];
+
+namespace flb200 {
+namespace {
+
+constexpr int kNoallocMaxDevices = 64;
+std::atomic<void*> g_noalloc_addr[kNoallocMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Device address of g_noalloc_scratch on the current device (looked up on
+// the first call per device, with that device current, then cached).
+int noalloc_scratch(void** addr) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kNoallocMaxDevices) {
+    if (e != cudaSuccess) set_last_cuda_error(e);
+    (void)cudaGetLastError();
+    return FL_B200_ERR_NO_DEVICE;
+  }
+  void* p = g_noalloc_addr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    p = g_noalloc_addr[dev].load(std::memory_order_relaxed);
+    if (p == nullptr) {
+      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess || p == nullptr) {
+        set_last_cuda_error(e);
+        (void)cudaGetLastError();
+        return FL_B200_ERR_LAUNCH;
+      }
+      g_noalloc_addr[dev].store(p, std::memory_order_release);
+    }
+  }
+  *addr = p;
+  return FL_B200_OK;
+}
+
+}  // namespace
+}  // namespace flb200
+
+extern "C" FL_B200_API int fl_b200_reduce_sum_all_noalloc(const void* x, int64_t n,
+                                                          void* out, int in_dtype,
+                                                          int out_dtype,
+                                                          fl_b200_stream_t stream) {
+  using namespace flb200;
+  FLB_CHECK_ARG(n >= 0);
+  // The split this sum will use must fit the fixed scratch.
+  const Plan plan = make_plan(1, n);
+  if (plan.ws_bytes > (size_t)FL_B200_NOALLOC_SCRATCH_BYTES) return FL_B200_ERR_TOO_LARGE;
+  void* scratch = nullptr;
+  if (plan.ws_bytes > 0) {
+    const int st = noalloc_scratch(&scratch);
+    if (st != FL_B200_OK) return st;
+  }
+  // Same kernel and split as fl_b200_reduce_sum_all; the scratch stands in for
+  // the caller's workspace (its ticket counters are zeroed on the stream).
+  return float_reduce_entry<kFinalSum>(x, n, 1, n, out, in_dtype, out_dtype, scratch,
+                                       FL_B200_NOALLOC_SCRATCH_BYTES,
+                                       static_cast<cudaStream_t>(stream));
+}

@@ -65,6 +65,7 @@ PROTOTYPES: dict[str, tuple] = {
     "fl_b200_reduce_middim": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _i32, _i32, _p]),
     "fl_b200_argmax_lastdim": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _p, _sz, _p]),
     "fl_b200_sum_i32_i64": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _p, _sz, _p]),
+    "fl_b200_reduce_sum_all_noalloc": (_i32, [_p, _i64, _p, _i32, _i32, _p]),
 }
 
 

@@ -198,7 +198,7 @@ FL_B200_API int fl_b200_softmax_middim(const void* x, void* out, int64_t outer,
  * 32-66), mean.dim (register.cc:248-252 -> mean.cu:30-63) and the          *
  * unregistered amax / argmax that the reference sends to the CPU fallback  *
  * (register.cc:439-442 -> fallback.cc:12-14).                              *
- * in_dtype F32/BF16/F16 (sum/mean also I32 -> out I64); float sums          *
+ * in_dtype F32/BF16/F16; sum also I32/I64 -> out I64 (exact); float sums   *
  * accumulate in fp32 inside a CTA and in fp64 across CTAs, so results are  *
  * deterministic run to run.  amax propagates NaN.                          *
  *                                                                           *

@@ -7,14 +7,16 @@
   ``torch_fl/_C*.so`` (linked against libfl_b200.so through an $ORIGIN rpath).
 * ``build_all()`` -- both.
 
-Every step is incremental: a target is rebuilt only when a source or header
-it depends on is newer than it.
+Every step is incremental: a target is rebuilt only when the content of a
+source, header or flag it depends on changed (hash stamps next to it).
 """
 
 from __future__ import annotations
 
 import concurrent.futures as _cf
 import glob
+import hashlib
+import importlib.util
 import os
 import shutil
 import subprocess
@@ -51,12 +53,28 @@ def _nvcc() -> str:
     return found
 
 
-def _newer(target: str, deps: list[str]) -> bool:
-    """True if target is missing or older than any dependency."""
-    if not os.path.exists(target):
+def _digest(paths: list[str], extra: str = "") -> str:
+    h = hashlib.sha256(extra.encode())
+    for p in paths:
+        h.update(os.path.basename(p).encode())
+        with open(p, "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
+def _stale(target: str, digest: str) -> bool:
+    """True unless `target` exists and was built from inputs with `digest`
+    (content hashes, so copies of the tree that lose mtimes stay valid)."""
+    stamp = target + ".stamp"
+    if not (os.path.exists(target) and os.path.exists(stamp)):
         return True
-    t = os.path.getmtime(target)
-    return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
+    with open(stamp) as f:
+        return f.read() != digest
+
+
+def _stamp(target: str, digest: str) -> None:
+    with open(target + ".stamp", "w") as f:
+        f.write(digest)
 
 
 def _run(cmd: list[str]) -> None:
@@ -77,37 +95,41 @@ def build_kernels(verbose: bool = False, jobs: int | None = None) -> str:
     headers = sorted(glob.glob(os.path.join(KERNEL_DIR, "*.cuh"))) + [
         os.path.join(INCLUDE_DIR, "fl_b200.h")
     ]
-    objs = []
-    todo = []
+    flags = " ".join(NVCC_FLAGS)
+    objs, todo = [], []
     for src in sources:
         obj = os.path.join(obj_dir, os.path.basename(src)[:-3] + ".o")
         objs.append(obj)
-        if _newer(obj, [src] + headers):
-            todo.append(
-                [nvcc, *NVCC_FLAGS, "-I", INCLUDE_DIR, "-c", src, "-o", obj]
-            )
+        dg = _digest([src] + headers, flags)
+        if _stale(obj, dg):
+            todo.append((obj, dg, [nvcc, *NVCC_FLAGS, "-I", INCLUDE_DIR, "-c", src, "-o", obj]))
     if todo:
         n = jobs or min(len(todo), os.cpu_count() or 4)
         with _cf.ThreadPoolExecutor(max_workers=n) as ex:
-            for cmd, fut in [(c, ex.submit(_run, c)) for c in todo]:
+            futs = [(obj, dg, cmd, ex.submit(_run, cmd)) for obj, dg, cmd in todo]
+            for obj, dg, cmd, fut in futs:
                 fut.result()
+                _stamp(obj, dg)
                 if verbose:
                     print("[build] " + os.path.basename(cmd[-3]))
-    if _newer(KERNEL_LIB, objs):
-        _run([nvcc, *ARCH_FLAGS, "-shared", "-o", KERNEL_LIB, *objs])
+    link_dg = _digest(objs, "link")
+    if _stale(KERNEL_LIB, link_dg):
+        _run([nvcc, *ARCH_FLAGS, "-shared", "-Xlinker", "-soname=libfl_b200.so", "-o",
+              KERNEL_LIB, *objs])
+        _stamp(KERNEL_LIB, link_dg)
         if verbose:
             print("[build] linked " + KERNEL_LIB)
     return KERNEL_LIB
 
 
 def build_torch_ext(verbose: bool = False) -> str | None:
-    """Build the torch extension (flagos PrivateUse1 device) if its sources exist."""
-    sys.path.insert(0, PKG_DIR)
-    try:
-        from torch_fl import _build_ext  # noqa: WPS433 (local import by design)
-    finally:
-        sys.path.pop(0)
-    return _build_ext.build(verbose=verbose)
+    """Build torch_fl/_C (the flagos PrivateUse1 device layer).  The recipe is
+    loaded by path so that the torch_fl package itself is not imported."""
+    spec = importlib.util.spec_from_file_location(
+        "_fl_b200_build_ext", os.path.join(PKG_DIR, "torch_fl", "_build_ext.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.build(verbose=verbose)
 
 
 def build_all(verbose: bool = False) -> None:

@@ -1,0 +1,313 @@
+// The `b200` route: the routed aten ops on this library's sm_100a kernels
+// (libfl_b200.so, include/fl_b200.h).  Each kernel validates, allocates its
+// output through the flagos allocator, launches on the current stream of the
+// tensor's GPU and turns a non-zero status into a TORCH_CHECK.  There is no
+// CPU fallback: a dtype the kernels do not take is an error naming the op.
+#include <ATen/WrapDimUtils.h>
+#include <ATen/ExpandUtils.h>
+
+#include <algorithm>
+#include <numeric>
+
+#include "ops.h"
+#include "tensor_utils.h"
+
+namespace flb200::aten {
+namespace {
+
+constexpr int kAdd = 0, kMul = 1;
+
+int RequireDtype(at::ScalarType t, const char* op) {
+  const int c = B200Dtype(t);
+  TORCH_CHECK(c >= 0, op, " (b200 route): dtype ", t, " is not supported "
+              "(float32, bfloat16, float16, int32, int64)");
+  return c;
+}
+
+bool IsFloat(at::ScalarType t) {
+  return t == at::kFloat || t == at::kBFloat16 || t == at::kHalf;
+}
+
+at::Tensor AsType(const at::Tensor& t, at::ScalarType st) {
+  return t.scalar_type() == st ? t : t.to(st);
+}
+
+// ------------------------------------------------------------- add / mul --
+at::Tensor BinaryScalar(const at::Tensor& a, double s, int op, double alpha, at::ScalarType rt,
+                        const char* name) {
+  const int code = RequireDtype(rt, name);
+  at::Tensor x = AsType(a, rt).contiguous();
+  at::Tensor out = at::empty(x.sizes(), x.options());
+  GpuGuard g(x);
+  CheckB200(fl_b200_binary_scalar(x.data_ptr(), s, out.data_ptr(), x.numel(), op, alpha, code,
+                                  StreamOf(x)),
+            name);
+  return out;
+}
+
+at::Tensor Binary(const at::Tensor& a, const at::Tensor& b, double alpha, int op,
+                  const char* name) {
+  const at::ScalarType rt = at::result_type(a, b);
+  // aten keeps a 0-dim CPU operand in opmath (add.cu:67-76 in the reference)
+  if (IsCpuScalar(b) && !IsCpuScalar(a))
+    return BinaryScalar(a, b.item<double>(), op, alpha, rt, name);
+  if (IsCpuScalar(a) && !IsCpuScalar(b) && (op == kMul || alpha == 1.0))
+    return BinaryScalar(b, a.item<double>(), op, 1.0, rt, name);
+  TORCH_CHECK(a.device() == b.device() || IsCpuScalar(a),
+              name, ": expected both operands on the same device, got ", a.device(), " and ",
+              b.device());
+  const int code = RequireDtype(rt, name);
+  at::Tensor x = AsType(IsCpuScalar(a) ? a.to(b.device()) : a, rt);
+  at::Tensor y = AsType(b, rt);
+  const std::vector<int64_t> shape = at::infer_size(x.sizes(), y.sizes());
+  TORCH_CHECK(shape.size() <= 8, name, " (b200 route): at most 8 dims");
+  at::Tensor xe = x.expand(shape), ye = y.expand(shape);
+  at::Tensor out = at::empty(shape, x.options());
+  if (out.numel() == 0) return out;
+  const std::vector<int64_t> sa(xe.strides().begin(), xe.strides().end());
+  const std::vector<int64_t> sb(ye.strides().begin(), ye.strides().end());
+  GpuGuard g(out);
+  const int st = op == kAdd
+      ? fl_b200_add(xe.data_ptr(), sa.data(), ye.data_ptr(), sb.data(), out.data_ptr(),
+                    shape.data(), (int)shape.size(), alpha, code, StreamOf(out))
+      : fl_b200_mul(xe.data_ptr(), sa.data(), ye.data_ptr(), sb.data(), out.data_ptr(),
+                    shape.data(), (int)shape.size(), code, StreamOf(out));
+  CheckB200(st, name);
+  return out;
+}
+
+at::Tensor AddTensorB200(const at::Tensor& a, const at::Tensor& b, const at::Scalar& alpha) {
+  return Binary(a, b, alpha.toDouble(), kAdd, "add.Tensor");
+}
+at::Tensor AddScalarB200(const at::Tensor& a, const at::Scalar& s, const at::Scalar& alpha) {
+  const at::ScalarType rt = at::result_type(a, s);
+  return BinaryScalar(a, s.toDouble(), kAdd, alpha.toDouble(), rt, "add.Scalar");
+}
+at::Tensor MulTensorB200(const at::Tensor& a, const at::Tensor& b) {
+  return Binary(a, b, 1.0, kMul, "mul.Tensor");
+}
+at::Tensor MulScalarB200(const at::Tensor& a, const at::Scalar& s) {
+  const at::ScalarType rt = at::result_type(a, s);
+  return BinaryScalar(a, s.toDouble(), kMul, 1.0, rt, "mul.Scalar");
+}
+
+// ---------------------------------------------------------------- softmax --
+at::Tensor SoftmaxB200(const at::Tensor& self, int64_t dim, bool half_to_float) {
+  const char* name = "_softmax";
+  const at::ScalarType in = self.scalar_type();
+  TORCH_CHECK(IsFloat(in), name, " (b200 route): floating point input expected, got ", in);
+  TORCH_CHECK(!half_to_float || in != at::kFloat,
+              name, ": half_to_float is only for float16/bfloat16 input");
+  const at::ScalarType ot = half_to_float ? at::kFloat : in;
+  if (self.dim() == 0) return at::ones({}, self.options().dtype(ot));
+  dim = at::maybe_wrap_dim(dim, self.dim());
+  at::Tensor x = self.contiguous();
+  at::Tensor out = at::empty(x.sizes(), x.options().dtype(ot));
+  if (x.numel() == 0) return out;
+  GpuGuard g(x);
+  const int64_t n = x.size(dim);
+  if (dim == x.dim() - 1) {
+    const int64_t rows = x.numel() / n;
+    CheckB200(fl_b200_softmax_lastdim(x.data_ptr(), n, out.data_ptr(), n, rows, n,
+                                      B200Dtype(in), B200Dtype(ot), 0, 1, 0, StreamOf(x)),
+              name);
+  } else {
+    int64_t outer = 1, inner = 1;
+    for (int64_t d = 0; d < dim; ++d) outer *= x.size(d);
+    for (int64_t d = dim + 1; d < x.dim(); ++d) inner *= x.size(d);
+    CheckB200(fl_b200_softmax_middim(x.data_ptr(), out.data_ptr(), outer, n, inner,
+                                     B200Dtype(in), B200Dtype(ot), StreamOf(x)),
+              name);
+  }
+  return out;
+}
+
+// ------------------------------------------------------------- reductions --
+enum class Red { kSum, kMean, kAmax, kArgmax };
+
+struct Workspace {
+  at::Tensor buf;
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  Workspace(const at::Tensor& like, int64_t rows, int64_t cols) {
+    bytes = fl_b200_reduce_workspace_size(rows, cols);
+    if (bytes) {
+      buf = at::empty({(int64_t)bytes}, like.options().dtype(at::kByte));
+      ptr = buf.data_ptr();
+    }
+  }
+};
+
+// Sorted, unique, wrapped reduction dims; all dims when `dims` is empty.
+std::vector<int64_t> NormDims(const at::Tensor& x, at::IntArrayRef dims) {
+  std::vector<int64_t> d;
+  if (dims.empty()) {
+    d.resize(x.dim());
+    std::iota(d.begin(), d.end(), 0);
+    return d;
+  }
+  for (int64_t v : dims) d.push_back(at::maybe_wrap_dim(v, x.dim()));
+  std::sort(d.begin(), d.end());
+  d.erase(std::unique(d.begin(), d.end()), d.end());
+  return d;
+}
+
+std::vector<int64_t> OutShape(const at::Tensor& x, const std::vector<int64_t>& red, bool keepdim) {
+  std::vector<int64_t> s;
+  for (int64_t d = 0; d < x.dim(); ++d) {
+    const bool r = std::binary_search(red.begin(), red.end(), d);
+    if (!r) s.push_back(x.size(d));
+    else if (keepdim) s.push_back(1);
+  }
+  return s;
+}
+
+// One launch of the row reduction `kind` over x viewed as [rows, cols].
+void LaunchRows(Red kind, const at::Tensor& x, int64_t rows, int64_t cols, int64_t ld,
+                at::Tensor& out, int in_code, int out_code, const char* name) {
+  Workspace ws(x, rows, cols);
+  const auto s = StreamOf(x);
+  int st = FL_B200_OK;
+  switch (kind) {
+    case Red::kSum:
+      st = fl_b200_reduce_sum_lastdim(x.data_ptr(), ld, rows, cols, out.data_ptr(), in_code,
+                                      out_code, ws.ptr, ws.bytes, s);
+      break;
+    case Red::kMean:
+      st = fl_b200_reduce_mean_lastdim(x.data_ptr(), ld, rows, cols, out.data_ptr(), in_code,
+                                       out_code, ws.ptr, ws.bytes, s);
+      break;
+    case Red::kAmax:
+      st = fl_b200_reduce_amax_lastdim(x.data_ptr(), ld, rows, cols, out.data_ptr(), in_code,
+                                       ws.ptr, ws.bytes, s);
+      break;
+    case Red::kArgmax:
+      st = fl_b200_argmax_lastdim(x.data_ptr(), ld, rows, cols,
+                                  static_cast<int64_t*>(out.data_ptr()), in_code, ws.ptr,
+                                  ws.bytes, s);
+      break;
+  }
+  CheckB200(st, name);
+}
+
+// Reduces x over `red` (sorted dims) into a fresh tensor of `out_t`.
+at::Tensor Reduce(Red kind, const at::Tensor& self, const std::vector<int64_t>& red, bool keepdim,
+                  at::ScalarType out_t, const char* name) {
+  const int in_code = RequireDtype(self.scalar_type(), name);
+  const int out_code = RequireDtype(out_t, name);
+  at::Tensor out = at::empty(OutShape(self, red, keepdim), self.options().dtype(out_t));
+  GpuGuard g(self);
+  if (self.dim() == 0) {  // reducing a scalar is the identity
+    out.copy_(kind == Red::kArgmax ? at::zeros({}, out.options()) : self.to(out_t).reshape({}));
+    return out;
+  }
+  if (out.numel() == 0) return out;
+  const int64_t nd = self.dim();
+  // Trailing dims [k, nd) reduced on a contiguous tensor: one rows view.
+  const bool trailing = red.back() == nd - 1 && (int64_t)red.size() == nd - red.front() &&
+                        red.front() == nd - (int64_t)red.size();
+  if (trailing) {
+    at::Tensor x = self.contiguous();
+    int64_t cols = 1;
+    for (int64_t d : red) cols *= x.size(d);
+    const int64_t rows = cols ? x.numel() / cols : out.numel();
+    LaunchRows(kind, x, rows, cols, std::max<int64_t>(cols, 1), out, in_code, out_code, name);
+    return out;
+  }
+  // One middle dim of a float tensor: reduce in place over [outer, n, inner].
+  if (red.size() == 1 && kind != Red::kArgmax && IsFloat(self.scalar_type()) &&
+      IsFloat(out_t)) {
+    at::Tensor x = self.contiguous();
+    const int64_t d = red[0];
+    int64_t outer = 1, inner = 1;
+    for (int64_t i = 0; i < d; ++i) outer *= x.size(i);
+    for (int64_t i = d + 1; i < nd; ++i) inner *= x.size(i);
+    const int op = kind == Red::kSum ? 0 : (kind == Red::kMean ? 1 : 2);
+    CheckB200(fl_b200_reduce_middim(x.data_ptr(), outer, x.size(d), inner, out.data_ptr(), op,
+                                    in_code, out_code, StreamOf(x)),
+              name);
+    return out;
+  }
+  // Anything else: move the reduced dims last, then one rows reduction.
+  std::vector<int64_t> perm;
+  for (int64_t d = 0; d < nd; ++d)
+    if (!std::binary_search(red.begin(), red.end(), d)) perm.push_back(d);
+  for (int64_t d : red) perm.push_back(d);
+  at::Tensor x = self.permute(perm).contiguous();
+  int64_t cols = 1;
+  for (int64_t d : red) cols *= self.size(d);
+  const int64_t rows = out.numel();
+  LaunchRows(kind, x, rows, cols, std::max<int64_t>(cols, 1), out, in_code, out_code, name);
+  return out;
+}
+
+at::Tensor SumDimB200(const at::Tensor& self, at::OptionalIntArrayRef dim, bool keepdim,
+                      std::optional<at::ScalarType> dtype) {
+  const char* name = "sum.dim_IntList";
+  at::ScalarType in = self.scalar_type();
+  const bool integral = at::isIntegralType(in, /*includeBool=*/true);
+  const at::ScalarType out_t = dtype ? *dtype : (integral ? at::kLong : in);
+  at::Tensor x = self;
+  if (integral) {
+    TORCH_CHECK(out_t == at::kLong, name, " (b200 route): integer sums produce int64");
+    if (in != at::kInt && in != at::kLong) x = self.to(at::kInt);  // bool/int8/int16: exact
+  } else {
+    TORCH_CHECK(IsFloat(in) && IsFloat(out_t), name, " (b200 route): dtype ", in, " -> ", out_t,
+                " is not supported");
+  }
+  const auto red = NormDims(x, dim.value_or(at::IntArrayRef{}));
+  return Reduce(Red::kSum, x, red, keepdim, out_t, name);
+}
+
+at::Tensor MeanDimB200(const at::Tensor& self, at::OptionalIntArrayRef dim, bool keepdim,
+                       std::optional<at::ScalarType> dtype) {
+  const char* name = "mean.dim";
+  const at::ScalarType out_t = dtype ? *dtype : self.scalar_type();
+  TORCH_CHECK(IsFloat(self.scalar_type()) && IsFloat(out_t),
+              "mean(): could not infer output dtype. Input dtype must be either a floating "
+              "point or complex dtype. Got: ", self.scalar_type());
+  const auto red = NormDims(self, dim.value_or(at::IntArrayRef{}));
+  return Reduce(Red::kMean, self, red, keepdim, out_t, name);
+}
+
+at::Tensor AmaxB200(const at::Tensor& self, at::IntArrayRef dim, bool keepdim) {
+  const char* name = "amax";
+  TORCH_CHECK(IsFloat(self.scalar_type()), name, " (b200 route): dtype ", self.scalar_type(),
+              " is not supported (float32, bfloat16, float16)");
+  const auto red = NormDims(self, dim);
+  for (int64_t d : red)
+    TORCH_CHECK(self.size(d) > 0, "amax(): Expected reduction dim ", d, " to have non-zero size.");
+  return Reduce(Red::kAmax, self, red, keepdim, self.scalar_type(), name);
+}
+
+at::Tensor ArgmaxB200(const at::Tensor& self, std::optional<int64_t> dim, bool keepdim) {
+  const char* name = "argmax";
+  TORCH_CHECK(IsFloat(self.scalar_type()), name, " (b200 route): dtype ", self.scalar_type(),
+              " is not supported (float32, bfloat16, float16)");
+  if (!dim) {
+    TORCH_CHECK(self.numel() > 0, "argmax(): Expected reduction dim to be specified for "
+                "input.numel() == 0.");
+    at::Tensor flat = self.reshape({-1});
+    at::Tensor r = Reduce(Red::kArgmax, flat, {0}, false, at::kLong, name);
+    return keepdim ? r.reshape(std::vector<int64_t>(self.dim(), 1)) : r;
+  }
+  const int64_t d = at::maybe_wrap_dim(*dim, std::max<int64_t>(self.dim(), 1));
+  if (self.dim() > 0)
+    TORCH_CHECK(self.size(d) > 0, "argmax(): Expected reduction dim ", d,
+                " to have non-zero size.");
+  return Reduce(Red::kArgmax, self, {d}, keepdim, at::kLong, name);
+}
+
+}  // namespace
+
+FLB_REGISTER_KERNEL(AddTensorFn, add_tensor_dispatcher, Backend::kB200, AddTensorB200)
+FLB_REGISTER_KERNEL(AddScalarFn, add_scalar_dispatcher, Backend::kB200, AddScalarB200)
+FLB_REGISTER_KERNEL(MulTensorFn, mul_tensor_dispatcher, Backend::kB200, MulTensorB200)
+FLB_REGISTER_KERNEL(MulScalarFn, mul_scalar_dispatcher, Backend::kB200, MulScalarB200)
+FLB_REGISTER_KERNEL(SoftmaxFn, softmax_dispatcher, Backend::kB200, SoftmaxB200)
+FLB_REGISTER_KERNEL(ReduceDimFn, sum_dim_dispatcher, Backend::kB200, SumDimB200)
+FLB_REGISTER_KERNEL(ReduceDimFn, mean_dim_dispatcher, Backend::kB200, MeanDimB200)
+FLB_REGISTER_KERNEL(AmaxFn, amax_dispatcher, Backend::kB200, AmaxB200)
+FLB_REGISTER_KERNEL(ArgmaxFn, argmax_dispatcher, Backend::kB200, ArgmaxB200)
+
+}  // namespace flb200::aten

@@ -112,6 +112,9 @@ __device__ __forceinline__ void fold_pack(typename P::Acc& acc, const uint4& u, 
     const int32_t w[4] = {(int32_t)u.x, (int32_t)u.y, (int32_t)u.z, (int32_t)u.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) P::fold(acc, (long long)w[e], j0 + e);
+  } else if constexpr (std::is_same<T, int64_t>::value) {
+    P::fold(acc, (long long)(((uint64_t)u.y << 32) | u.x), j0);
+    P::fold(acc, (long long)(((uint64_t)u.w << 32) | u.z), j0 + 1);
   } else {
     constexpr int VW = Elem<T>::kVec;
     float f[VW];
@@ -123,13 +126,14 @@ __device__ __forceinline__ void fold_pack(typename P::Acc& acc, const uint4& u, 
 
 template <typename T, typename P>
 __device__ __forceinline__ void fold_scalar(typename P::Acc& acc, const T* p, int64_t j) {
-  if constexpr (std::is_same<T, int32_t>::value) P::fold(acc, (long long)*p, j);
+  if constexpr (std::is_integral<T>::value) P::fold(acc, (long long)*p, j);
   else P::fold(acc, elem_value<T>(*p), j);
 }
 
 template <typename T>
 __host__ __device__ constexpr int pack_width() {
   if constexpr (std::is_same<T, int32_t>::value) return 4;
+  else if constexpr (std::is_same<T, int64_t>::value) return 2;
   else return Elem<T>::kVec;
 }
 
@@ -333,9 +337,13 @@ int float_reduce_entry(const void* x, int64_t ld, int64_t rows, int64_t cols, vo
   if (rows == 0) return FL_B200_OK;
   FLB_CHECK_ARG(x || cols == 0);
   FLB_CHECK_ARG(out && ld >= cols);
-  if (in_dtype == FL_B200_I32 && (FINAL == kFinalSum) && out_dtype == FL_B200_I64) {
+  if ((in_dtype == FL_B200_I32 || in_dtype == FL_B200_I64) && FINAL == kFinalSum &&
+      out_dtype == FL_B200_I64) {
     if (cols == 0) return cudaMemsetAsync(out, 0, rows * 8, stream) == cudaSuccess
                               ? FL_B200_OK : FL_B200_ERR_LAUNCH;
+    if (in_dtype == FL_B200_I64)
+      return launch_reduce<int64_t, IntSumPolicy, kFinalI64>(
+          static_cast<const int64_t*>(x), ld, rows, cols, out, out_dtype, ws, ws_bytes, stream);
     return launch_reduce<int32_t, IntSumPolicy, kFinalI64>(
         static_cast<const int32_t*>(x), ld, rows, cols, out, out_dtype, ws, ws_bytes, stream);
   }

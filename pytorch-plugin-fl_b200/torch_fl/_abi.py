@@ -82,11 +82,9 @@ class FlB200Error(RuntimeError):
 _LIB: C.CDLL | None = None
 
 
-def load(path: str = LIB_PATH) -> C.CDLL:
-    """Load the kernel library (once) and attach the prototypes."""
-    global _LIB
-    if _LIB is not None:
-        return _LIB
+def open_library(path: str) -> C.CDLL:
+    """Open a libfl_b200.so and attach the prototypes; a missing file is an
+    error (the b200 route has no fallback)."""
     if not os.path.exists(path):
         raise FileNotFoundError(
             f"{path} is missing: build it with `python pytorch-plugin-fl_b200/build.py` "
@@ -97,8 +95,15 @@ def load(path: str = LIB_PATH) -> C.CDLL:
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
-    _LIB = lib
     return lib
+
+
+def load(path: str = LIB_PATH) -> C.CDLL:
+    """Load the kernel library (once per process)."""
+    global _LIB
+    if _LIB is None:
+        _LIB = open_library(path)
+    return _LIB
 
 
 def lib() -> C.CDLL:

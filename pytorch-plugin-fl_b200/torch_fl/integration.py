@@ -1,0 +1,131 @@
+"""Operator registration helpers and the HuggingFace fused-op hooks.
+
+`register_flagos_operator` keeps the reference's API
+(torch_fl/integration.py:33-49 there): register a Python implementation of an
+aten op for the flagos device.
+
+`enable_hf_fused_ops()` is the site the reference lacks (it has no HF hooks):
+it replaces, in the installed transformers, the forward of the RMSNorm
+modules, the module-level `apply_rotary_pos_emb`, and the SwiGLU MLP forward
+of the Qwen3 / Qwen2 / Llama / Mistral model files with the flagos:: fused
+kernels.  The hooks act on device tensors (flagos or cuda) that need no
+gradient; anything else (CPU tensors, training with autograd) runs the
+original HF code unchanged.  `disable_hf_fused_ops()` restores the originals.
+"""
+
+from __future__ import annotations
+
+import importlib
+from typing import Callable, Optional
+
+import torch
+
+from . import ops
+
+_registered_ops: set = set()
+_libs: list = []
+
+
+def register_flagos_operator(op_name: str, impl_func: Callable, schema: Optional[str] = None) -> None:
+    """Register `impl_func` as the flagos (PrivateUse1) kernel of aten op
+    `op_name` (e.g. "add.Tensor"); with `schema`, define it first."""
+    lib = torch.library.Library("aten", "IMPL") if schema is None else torch.library.Library(
+        "aten", "FRAGMENT")
+    if schema is not None:
+        lib.define(schema)
+    lib.impl(op_name, impl_func, "PrivateUse1")
+    _registered_ops.add(op_name)
+    _libs.append(lib)
+
+
+def get_registered_ops() -> list:
+    return sorted(_registered_ops)
+
+
+# ------------------------------------------------------------- HF fused hooks
+_MODEL_FILES = {
+    "qwen3": ("Qwen3RMSNorm", "Qwen3MLP"),
+    "qwen2": ("Qwen2RMSNorm", "Qwen2MLP"),
+    "llama": ("LlamaRMSNorm", "LlamaMLP"),
+    "mistral": ("MistralRMSNorm", "MistralMLP"),
+}
+_saved: dict = {}
+_rounding: Optional[str] = None
+
+
+def _fusable(*tensors) -> bool:
+    for t in tensors:
+        if not isinstance(t, torch.Tensor) or t.device.type not in ("flagos", "privateuseone",
+                                                                     "cuda"):
+            return False
+        if t.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+            return False
+    return not (torch.is_grad_enabled() and any(t.requires_grad for t in tensors))
+
+
+def _rms_forward(orig):
+    def forward(self, hidden_states):
+        w = self.weight
+        if _fusable(hidden_states, w) and w.dtype == hidden_states.dtype:
+            return ops.rms_norm(hidden_states, w, self.variance_epsilon, _rounding)
+        return orig(self, hidden_states)
+
+    forward.__wrapped__ = orig
+    return forward
+
+
+def _rope_fn(orig):
+    def apply_rotary_pos_emb(q, k, cos, sin, *args, **kwargs):
+        unsqueeze_dim = kwargs.get("unsqueeze_dim", args[-1] if args and isinstance(args[-1], int) else 1)
+        if (_fusable(q, k, cos, sin) and q.dim() == 4 and q.dtype == cos.dtype == k.dtype
+                and unsqueeze_dim in (1, 2)):
+            return ops.rope_qk(q, k, cos, sin, unsqueeze_dim, _rounding)
+        return orig(q, k, cos, sin, *args, **kwargs)
+
+    apply_rotary_pos_emb.__wrapped__ = orig
+    return apply_rotary_pos_emb
+
+
+def _mlp_forward(orig):
+    def forward(self, x):
+        act = getattr(self, "act_fn", None)
+        is_silu = isinstance(act, torch.nn.SiLU) or type(act).__name__ in ("SiLUActivation", "SiLU")
+        if is_silu and _fusable(x):
+            return self.down_proj(ops.swiglu(self.gate_proj(x), self.up_proj(x), _rounding))
+        return orig(self, x)
+
+    forward.__wrapped__ = orig
+    return forward
+
+
+def enable_hf_fused_ops(models=tuple(_MODEL_FILES), rounding: Optional[str] = None) -> list:
+    """Patch the installed transformers model files; returns what was patched."""
+    global _rounding
+    _rounding = rounding
+    patched = []
+    for name in models:
+        try:
+            mod = importlib.import_module(f"transformers.models.{name}.modeling_{name}")
+        except Exception:
+            continue
+        norm_cls, mlp_cls = _MODEL_FILES[name]
+        targets = [(getattr(mod, norm_cls, None), "forward", _rms_forward),
+                   (getattr(mod, mlp_cls, None), "forward", _mlp_forward),
+                   (mod, "apply_rotary_pos_emb", _rope_fn)]
+        for owner, attr, make in targets:
+            if owner is None or not hasattr(owner, attr):
+                continue
+            key = (id(owner), attr)
+            if key in _saved:
+                continue
+            orig = getattr(owner, attr)
+            _saved[key] = (owner, attr, orig)
+            setattr(owner, attr, make(orig))
+            patched.append(f"{getattr(owner, '__name__', owner)}.{attr}")
+    return patched
+
+
+def disable_hf_fused_ops() -> None:
+    for owner, attr, orig in _saved.values():
+        setattr(owner, attr, orig)
+    _saved.clear()

@@ -1,0 +1,90 @@
+"""HuggingFace models on the flagos device, with and without the fused-op
+hooks (torch_fl.enable_hf_fused_ops).  A small random-init Qwen3 (the
+reference's e2e tests use Qwen3-0.6B weights, which are not available here)
+runs its forward on flagos:0 and is compared with the same model on the CPU.
+"""
+
+import pytest
+import torch
+
+import torch_fl
+from torch_fl import integration
+
+pytestmark = pytest.mark.gpu
+
+
+def tiny_qwen3(dtype):
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    cfg = Qwen3Config(vocab_size=512, hidden_size=256, intermediate_size=704,
+                      num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                      head_dim=64, max_position_embeddings=256, rms_norm_eps=1e-6,
+                      attn_implementation="eager")
+    torch.manual_seed(0)
+    m = Qwen3ForCausalLM(cfg).to(dtype).eval()
+    return m
+
+
+@pytest.fixture(autouse=True)
+def _no_hooks_after():
+    yield
+    torch_fl.disable_hf_fused_ops()
+
+
+def test_qwen3_forward_on_flagos_matches_cpu():
+    model = tiny_qwen3(torch.float32)
+    ids = torch.randint(0, 512, (2, 48), generator=torch.Generator().manual_seed(1))
+    with torch.no_grad():
+        ref = model(ids).logits
+        model_d = model.to("flagos:0")
+        out = model_d(ids.to("flagos:0")).logits
+    assert out.device.type == "flagos"
+    torch.testing.assert_close(out.cpu(), ref, rtol=1e-3, atol=1e-3)
+
+
+def test_qwen3_forward_with_fused_hooks(monkeypatch):
+    calls = {"rms_norm": 0, "rope_qk": 0, "swiglu": 0}
+    for name in calls:
+        orig = getattr(torch_fl.ops, name)
+
+        def counted(*a, _orig=orig, _name=name, **k):
+            calls[_name] += 1
+            return _orig(*a, **k)
+
+        monkeypatch.setattr(torch_fl.ops, name, counted)
+    model = tiny_qwen3(torch.float32)
+    ids = torch.randint(0, 512, (2, 48), generator=torch.Generator().manual_seed(2))
+    with torch.no_grad():
+        ref = model(ids).logits
+        model_d = model.to("flagos:0")
+        patched = torch_fl.enable_hf_fused_ops()
+        assert any("apply_rotary_pos_emb" in p for p in patched)
+        out = model_d(ids.to("flagos:0")).logits
+    # 2 layers x (input + post-attention + q_norm + k_norm) + final norm
+    assert calls["rms_norm"] >= 9 and calls["rope_qk"] == 2 and calls["swiglu"] == 2, calls
+    torch.testing.assert_close(out.cpu(), ref, rtol=1e-3, atol=1e-3)
+
+
+def test_qwen3_bf16_hooks_match_unhooked():
+    model = tiny_qwen3(torch.bfloat16).to("flagos:0")
+    ids = torch.randint(0, 512, (1, 64), generator=torch.Generator().manual_seed(3)).to("flagos:0")
+    with torch.no_grad():
+        plain = model(ids).logits.float().cpu()
+        torch_fl.enable_hf_fused_ops(rounding="chain")
+        chain = model(ids).logits.float().cpu()
+        torch_fl.disable_hf_fused_ops()
+        torch_fl.enable_hf_fused_ops(rounding="fused")
+        fused = model(ids).logits.float().cpu()
+    scale = plain.abs().max()
+    assert (chain - plain).abs().max() <= 0.05 * scale
+    assert (fused - plain).abs().max() <= 0.05 * scale
+
+
+def test_hooks_leave_cpu_and_autograd_paths_alone():
+    model = tiny_qwen3(torch.float32)
+    torch_fl.enable_hf_fused_ops()
+    ids = torch.randint(0, 512, (1, 16))
+    out = model(ids).logits          # CPU tensors: the original HF code runs
+    out.sum().backward()             # and autograd works
+    assert model.model.norm.weight.grad is not None
+    integration.disable_hf_fused_ops()

@@ -11,10 +11,13 @@ layers (the bytes moved are the same as with fresh activations per layer).
 Outputs ONE JSON line (rank 0):
   value     tokens/s of the whole job, inputs resident in HBM, device time
             (CUDA events), max over ranks.
-  e2e       the same metric through the public API with the hidden state
-            copied host->device before and device->host after every step.
-  roofline  the dominant kernel (SwiGLU + residual add) against the measured
-            HBM copy bandwidth.
+  e2e       the same metric through the reference-facing plugin API (flagos
+            tensors, torch_fl.ops) with the hidden state copied from pinned
+            host memory before and back after every step.
+  roofline  the kernel with the largest total time (SwiGLU) against the
+            measured HBM copy bandwidth.
+  gpu_eager_reference  the HF formulas on PyTorch's own CUDA kernels (what
+            the reference's cuda route runs) on the same stack, N=1.
   per_op    achieved HBM GB/s of every kernel of the step (CUDA events
             around each launch inside the timed region).
   cpu_baseline  the reference's CPU path (HF formulas on torch CPU aten) on
@@ -211,6 +214,56 @@ class Stack:
             x, nxt = nxt, (self.xb if nxt is self.xa else self.xa)
         return x
 
+    # ---- the same stack through the public plugin API on flagos tensors ----
+    def flagos_views(self):
+        """Zero-copy flagos views of the rank's buffers (flagos memory is
+        CUDA memory of the same GPU)."""
+        from torch_fl import _C
+
+        v = _C._cuda_to_flagos_view
+        self.fq, self.fk, self.fg, self.fu, self.fy = (v(t) for t in (self.q, self.k, self.g,
+                                                                      self.u, self.y))
+        self.fcos, self.fsin = v(self.cos), v(self.sin)
+        self.fw = [v(w) for w in self.w]
+
+    def run_flagos(self, x):
+        """One step through torch_fl.ops (flagos:: ops through PyTorch's
+        dispatcher, outputs allocated by the flagos allocator)."""
+        import torch_fl.ops as O
+
+        r = self.rounding
+        n = O.rms_norm(x, self.fw[0], EPS, r)
+        for l in range(self.L):
+            qo, ko = O.rope_qk(self.fq, self.fk, self.fcos, self.fsin, 2, r)
+            if l + 1 < self.L:
+                a = O.swiglu(self.fg, self.fu, r)
+                n, x = O.add_rms_norm(x, self.fy, self.fw[l + 1], EPS, r)
+            else:
+                a, x = O.swiglu_residual(self.fg, self.fu, x, self.fy, r)
+        return x
+
+    def run_torch_eager(self, x, layers):
+        """`layers` layers of the HF formulas on PyTorch's own CUDA kernels
+        (the kernels the reference's cuda route runs): RMSNorm
+        (modeling_qwen3.py:59-64), apply_rotary_pos_emb (:158-181),
+        silu(gate) * up (:81-82), residual add."""
+        q = self.q.transpose(1, 2)        # [B, H, S, D] view, as HF passes it
+        k = self.k.transpose(1, 2)
+        cos, sin = self.cos[None, None], self.sin[None, None]
+
+        def rotate_half(t):
+            return torch.cat((-t[..., HEAD // 2:], t[..., :HEAD // 2]), dim=-1)
+
+        for l in range(layers):
+            h = x.to(torch.float32)
+            h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + EPS)
+            n = self.w[l] * h.to(x.dtype)
+            qe = (q * cos) + (rotate_half(q) * sin)
+            ke = (k * cos) + (rotate_half(k) * sin)
+            a = torch.nn.functional.silu(self.g) * self.u
+            x = x + self.y
+        return x, n, qe, ke, a
+
     def _rope(self):
         self.K.rope_qk(self.q, self.k, self.cos, self.sin, layout="bshd", rounding=self.rounding,
                        q_out=self.qo, k_out=self.ko)
@@ -319,6 +372,8 @@ def main():
     ap.add_argument("--cpu-reps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-eager", action="store_true")
+    ap.add_argument("--eager-layers", type=int, default=4)
     args = ap.parse_args()
     assert args.warmup >= 3 or os.environ.get("FL_B200_BENCH_ALLOW_SHORT"), "use --warmup >= 3"
 
@@ -349,6 +404,7 @@ def main():
 
     import torch_fl  # noqa: F401  (loads libfl_b200.so; fails loudly if missing)
     from torch_fl import kernels as K
+    from torch_fl import sharding
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -389,13 +445,7 @@ def main():
     torch.cuda.synchronize()
     barrier()
     clock_info = clocks.stop()
-    ms = start.elapsed_time(end)
-    if world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = sharding.max_over_ranks(start.elapsed_time(end), dev)
     ms_per_step = ms / args.steps
     value = args.tokens * args.steps / (ms / 1e3)
 
@@ -422,37 +472,57 @@ def main():
                 else "fallback", "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "traffic": traffic, "algorithmic_bytes": dom_bytes}
 
-    # end to end through the public API, host buffers, copies inside the timed region
+    # End to end through the reference-facing plugin API: the hidden state
+    # comes from pinned host memory into a flagos tensor, the 32 layers run as
+    # torch_fl.ops (flagos:: ops through PyTorch's dispatcher, outputs from
+    # the flagos allocator), the result goes back to host memory; all inside
+    # the timed region, on the flagos device's current stream.
     e2e = None
     if not args.no_e2e:
+        fdev = torch.device("flagos", local)
+        stack.flagos_views()
         h_in = torch.empty(T, HIDDEN, dtype=torch.bfloat16, pin_memory=True)
         h_in.copy_(stack.x0)
         h_out = torch.empty_like(h_in, pin_memory=True)
-        d_in = torch.empty_like(stack.x0)
         for _ in range(2):
-            d_in.copy_(h_in, non_blocking=True)
-            h_out.copy_(stack.run(d_in), non_blocking=True)
+            h_out.copy_(stack.run_flagos(h_in.to(fdev, non_blocking=True)), non_blocking=True)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(args.steps):
-            d_in.copy_(h_in, non_blocking=True)
-            res = stack.run(d_in)
+            x_d = h_in.to(fdev, non_blocking=True)
+            res = stack.run_flagos(x_d)
             h_out.copy_(res, non_blocking=True)
         e1.record()
         torch.cuda.synchronize()
-        ems = e0.elapsed_time(e1)
-        if world > 1:
-            import torch.distributed as dist
-
-            t = torch.tensor([ems], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ems = float(t.item())
+        ems = sharding.max_over_ranks(e0.elapsed_time(e1), dev)
+        # the e2e result equals the device-resident path's result
+        same = bool(torch.equal(h_out.to(dev), stack.run(stack.x0)))
         nbytes = h_in.numel() * h_in.element_size()
         e2e = {"value": args.tokens * args.steps / (ems / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
-               "ms_per_step": ems / args.steps,
-               "api": "torch_fl.kernels (C ABI of libfl_b200.so) on device tensors"}
+               "h2d_bytes_per_step": nbytes * world, "d2h_bytes_per_step": nbytes * world,
+               "ms_per_step": ems / args.steps, "matches_device_path": same,
+               "api": "torch_fl.ops (flagos:: ops) on flagos tensors, host<->flagos copies"}
+
+    # PyTorch's own CUDA kernels on the HF formulas (the kernels the
+    # reference's cuda route runs), same stack, `eager_layers` layers timed
+    # and scaled to the full depth; informational.
+    eager = None
+    if not args.no_eager and world == 1:
+        L = min(args.eager_layers, args.layers)
+        for _ in range(2):
+            stack.run_torch_eager(stack.x0, L)
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(2):
+            stack.run_torch_eager(stack.x0, L)
+        g1.record()
+        torch.cuda.synchronize()
+        ms_layer = g0.elapsed_time(g1) / (2 * L)
+        eager = {"value": T / (ms_layer * args.layers / 1e3), "unit": "tokens/s",
+                 "ms_per_layer": ms_layer, "layers_timed": L,
+                 "what": f"HF formulas on torch {torch.__version__} CUDA eager kernels, bf16"}
 
     # correctness gather (NCCL, outside the timed region): sampled rows of
     # every rank checked on rank 0 against the oracle
@@ -477,6 +547,7 @@ def main():
                        "l2": "inputs larger than L2 (every per-rank activation >= 256 MB)"},
             "hbm_gbs_step": round(stack_bytes(stack) * args.steps / (ms / 1e3) / 1e9, 1),
             "per_op": per_op, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_eager_reference": eager,
             "gpu_launches": stack.launches_per_step() * args.steps,
             "clocks": clock_info, "correctness": check,
         }

@@ -236,10 +236,8 @@ cast_vec8_kernel(const S* src, D* dst, int64_t n8) {
 }
 
 template <typename K>
-int grid_for(K kern, int64_t work, const DeviceInfo& dev, int waves = 1) {
-  const int per_sm = blocks_per_sm(kern, kBlock, 0);
-  return (int)std::max<int64_t>(
-      1, std::min<int64_t>(ceil_div(work, kBlock), (int64_t)per_sm * dev.sm_count * waves));
+int grid_for(K, int64_t work, const DeviceInfo&, int = 1) {
+  return full_grid(ceil_div(work, kBlock));  // one unit of work per thread
 }
 
 template <typename F>
@@ -318,10 +316,8 @@ int binary_entry(const void* a, const int64_t* sa, const void* b, const int64_t*
       const bool b_dense = dense_strides(sz, sb_, ndim);
       if (a_dense && b_dense && n % VW == 0 && all_aligned) {
         auto kern = binary_dense_kernel<T, OP>;
-        static const int per_sm = blocks_per_sm(kern, kBlock, 0);
         const int64_t npk = n / VW;
-        const int grid = (int)std::max<int64_t>(
-            1, std::min<int64_t>(ceil_div(npk, kBlock), (int64_t)per_sm * dev.sm_count));
+        const int grid = full_grid(ceil_div(npk, kBlock));
         kern<<<grid, kBlock, 0, stream>>>(ap, bp, op, npk, al);
         return launch_status();
       }

@@ -316,9 +316,7 @@ int launch_reduce(const T* x, int64_t ld, int64_t rows, int64_t cols, void* out,
   const bool vec = aligned16(x) && ld % VW == 0 && cols % VW == 0 && plan.chunk % VW == 0;
   const int64_t units = rows * plan.splits;
   auto go = [&](auto kern) -> int {
-    const int per_sm = blocks_per_sm(kern, kBlock, 0);
-    const int grid = (int)std::max<int64_t>(
-        1, std::min<int64_t>(units, (int64_t)per_sm * dev.sm_count * 4));
+    const int grid = full_grid(units);  // one CTA per row chunk
     kern<<<grid, kBlock, 0, stream>>>(x, ld, rows, cols, plan.splits, plan.chunk, out,
                                       out_dtype, parts, tickets);
     return launch_status();
@@ -474,10 +472,7 @@ FL_B200_API int fl_b200_reduce_middim(const void* x, int64_t outer, int64_t n,
   return dispatch_float(in_dtype, [&](auto tag) -> int {
     using T = decltype(tag);
     auto run = [&](auto kern) -> int {
-      const int per_sm = blocks_per_sm(kern, kBlock, 0);
-      const int64_t units = outer * ceil_div(inner, 32);
-      const int grid = (int)std::max<int64_t>(
-          1, std::min<int64_t>(units, (int64_t)per_sm * dev.sm_count * 4));
+      const int grid = full_grid(outer * ceil_div(inner, 32));
       kern<<<grid, kBlock, 0, s>>>(static_cast<const T*>(x), outer, n, inner, out,
                                    out_dtype);
       return launch_status();

@@ -134,14 +134,15 @@ int launch_rms_norm(const T* x, int64_t ldx, const T* y, T* h, const T* w, T* ou
                       ldx % VW == 0 && ldo % VW == 0;
   if (vec_ok) {
     const int64_t nvec = cols / VW;
-    int r = row_ladder(nvec, [&](auto tpr, auto vpt) -> int {
+    // One CTA per group of rows (full grid); two input streams (ADD) want
+    // fewer packs per thread and more threads per row.
+    int r = row_ladder<ADD ? 2 : 8>(nvec, [&](auto tpr, auto vpt) -> int {
       constexpr int TPR = decltype(tpr)::value;
       constexpr int VPT = decltype(vpt)::value;
       constexpr int BLOCK = ladder_block<TPR>();
       auto kern = rms_norm_vec_kernel<T, TPR, VPT, BLOCK, CHAIN, ADD>;
-      static const int per_sm = blocks_per_sm(kern, BLOCK, 0);
       const int64_t units = ceil_div(rows, BLOCK / TPR);
-      const int grid = (int)std::min<int64_t>(units, (int64_t)per_sm * dev.sm_count);
+      const int grid = full_grid(units);
       kern<<<grid, BLOCK, 0, stream>>>(x, ldx, y, h, w, out, ldo, rows, (int)nvec, eps,
                                        (float)cols);
       return launch_status();

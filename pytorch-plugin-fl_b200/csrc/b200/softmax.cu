@@ -207,9 +207,7 @@ int launch_softmax(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
       constexpr int VPT = decltype(vpt)::value;
       constexpr int BLOCK = ladder_block<TPR>();
       auto kern = softmax_vec_kernel<TI, TO, TPR, VPT, BLOCK, CAUSAL>;
-      static const int per_sm = blocks_per_sm(kern, BLOCK, 0);
-      const int64_t units = ceil_div(rows, BLOCK / TPR);
-      const int grid = (int)std::min<int64_t>(units, (int64_t)per_sm * dev.sm_count);
+      const int grid = full_grid(ceil_div(rows, BLOCK / TPR));
       kern<<<grid, BLOCK, 0, stream>>>(x, ldx, y, ldy, rows, cols, q_len, offset);
       return launch_status();
     });

@@ -4,8 +4,8 @@
 // models/qwen3/modeling_qwen3.py:81-82), run on flagos as silu
 // (csrc/aten/backends/cuda/silu.cu:15-35: x / (1 + exp(-x)) in fp32 opmath,
 // rounded to the tensor dtype) followed by mul (mul.cu:28-52).  The residual
-// add is add.Tensor (add.cu:48-84).  Pure streaming: UNROLL packs per thread
-// per iteration keep enough loads in flight to saturate HBM.
+// add is add.Tensor (add.cu:48-84).  Pure streaming, launched as a full grid
+// (one 16-byte pack per thread; common.cuh full_grid).
 #include "common.cuh"
 
 #include <algorithm>
@@ -109,6 +109,47 @@ swiglu_residual_kernel(const T* g, const T* u, T* act, int64_t n_act, const T* x
   add_dense<T>(x, y, h, n_res, tid, nth);
 }
 
+// 32-byte packs (two 16-byte halves per access), one per thread: the path
+// for 32-byte aligned dense tensors.  The CTAs of the grid's first
+// `act_blocks` do SwiGLU packs, the rest residual-add packs (n_res may be 0).
+template <typename T, bool CHAIN>
+__global__ void __launch_bounds__(kBlock)
+swiglu32_kernel(const T* g, const T* u, T* act, int64_t n_act, int64_t act_blocks,
+                const T* x, const T* y, T* h, int64_t n_res) {
+  constexpr int VW2 = 2 * Elem<T>::kVec;  // elements per 32-byte pack
+  if ((int64_t)blockIdx.x < act_blocks) {
+    const int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x;
+    if (i < n_act) {
+      const Pack32 gv = ld_stream32(g + i * VW2), uv = ld_stream32(u + i * VW2);
+      Pack32 o;
+      o.lo = swiglu_pack<T, CHAIN>(gv.lo, uv.lo);
+      o.hi = swiglu_pack<T, CHAIN>(gv.hi, uv.hi);
+      st_stream32(act + i * VW2, o);
+    }
+  } else {
+    const int64_t i = ((int64_t)blockIdx.x - act_blocks) * kBlock + threadIdx.x;
+    if (i < n_res) {
+      const Pack32 xv = ld_stream32(x + i * VW2), yv = ld_stream32(y + i * VW2);
+      Pack32 o;
+      o.lo = add_pack<T>(xv.lo, yv.lo);
+      o.hi = add_pack<T>(xv.hi, yv.hi);
+      st_stream32(h + i * VW2, o);
+    }
+  }
+}
+
+template <typename T, bool CHAIN>
+int launch_swiglu32(const T* g, const T* u, T* act, int64_t n_act, const T* x, const T* y,
+                    T* h, int64_t n_res, cudaStream_t stream) {
+  constexpr int VW2 = 2 * Elem<T>::kVec;
+  const int64_t pa = n_act / VW2, pr = n_res / VW2;
+  const int64_t ba = ceil_div(pa, kBlock), br = ceil_div(pr, kBlock);
+  if (ba + br > 0x7fffffff) return FL_B200_ERR_TOO_LARGE;
+  swiglu32_kernel<T, CHAIN><<<(int)std::max<int64_t>(ba + br, 1), kBlock, 0, stream>>>(
+      g, u, act, pa, ba, x, y, h, pr);
+  return launch_status();
+}
+
 // Strided / unaligned rows: scalar element access.
 template <typename T, bool CHAIN>
 __global__ void __launch_bounds__(kBlock)
@@ -133,19 +174,17 @@ int launch_swiglu(const T* g, int64_t ldg, const T* u, int64_t ldu, T* o, int64_
   constexpr int VW = Elem<T>::kVec;
   const bool dense = ldg == cols && ldu == cols && ldo == cols;
   const int64_t n = rows * cols;
+  if (dense && n % (2 * VW) == 0 && aligned32(g) && aligned32(u) && aligned32(o))
+    return launch_swiglu32<T, CHAIN>(g, u, o, n, nullptr, nullptr, nullptr, 0, stream);
   if (dense && n % VW == 0 && aligned16(g) && aligned16(u) && aligned16(o)) {
     auto kern = swiglu_vec_kernel<T, CHAIN>;
-    static const int per_sm = blocks_per_sm(kern, kBlock, 0);
     const int64_t npk = n / VW;
-    const int grid = (int)std::max<int64_t>(
-        1, std::min<int64_t>(ceil_div(npk, kBlock), (int64_t)per_sm * dev.sm_count));
+    const int grid = full_grid(ceil_div(npk, kBlock));  // one pack per thread
     kern<<<grid, kBlock, 0, stream>>>(g, u, o, npk);
     return launch_status();
   }
   auto kern = swiglu_strided_kernel<T, CHAIN>;
-  static const int per_sm = blocks_per_sm(kern, kBlock, 0);
-  const int grid = (int)std::max<int64_t>(
-      1, std::min<int64_t>(ceil_div(n, kBlock), (int64_t)per_sm * dev.sm_count * 4));
+  const int grid = full_grid(ceil_div(n, kBlock));
   kern<<<grid, kBlock, 0, stream>>>(g, ldg, u, ldu, o, ldo, rows, cols);
   return launch_status();
 }
@@ -159,14 +198,15 @@ int launch_swiglu_residual(const T* g, const T* u, T* act, int64_t inter, const 
   if (st != FL_B200_OK) return st;
   constexpr int VW = Elem<T>::kVec;
   const int64_t n1 = rows * inter, n2 = rows * hidden;
+  if (n1 % (2 * VW) == 0 && n2 % (2 * VW) == 0 && aligned32(g) && aligned32(u) &&
+      aligned32(act) && aligned32(x) && aligned32(y) && aligned32(h))
+    return launch_swiglu32<T, CHAIN>(g, u, act, n1, x, y, h, n2, stream);
   const bool vec_ok = n1 % VW == 0 && n2 % VW == 0 && aligned16(g) && aligned16(u) &&
                       aligned16(act) && aligned16(x) && aligned16(y) && aligned16(h);
   if (!vec_ok) return FL_B200_ERR_MISALIGNED;
   auto kern = swiglu_residual_kernel<T, CHAIN>;
-  static const int per_sm = blocks_per_sm(kern, kBlock, 0);
   const int64_t npk = std::max(n1, n2) / VW;
-  const int grid = (int)std::max<int64_t>(
-      1, std::min<int64_t>(ceil_div(npk, kBlock), (int64_t)per_sm * dev.sm_count));
+  const int grid = full_grid(ceil_div(npk, kBlock));  // one pack of each part per thread
   kern<<<grid, kBlock, 0, stream>>>(g, u, act, n1 / VW, x, y, h, n2 / VW);
   return launch_status();
 }

@@ -157,8 +157,9 @@ class Stack:
         rank = _env_int("RANK", 0)
         g = torch.Generator(device=device)
 
-        def rn(seed, *shape, scale=1.0, loc=0.0):
-            g.manual_seed(seed + 100000 * rank)
+        def rn(seed, *shape, scale=1.0, loc=0.0, per_rank=True):
+            # activations: the rank's own rows; weights: the same on every rank
+            g.manual_seed(seed + (100000 * rank if per_rank else 0))
             return (loc + scale * torch.randn(*shape, generator=g, device=device)).to(torch.bfloat16)
 
         T = tokens
@@ -168,7 +169,8 @@ class Stack:
         self.g = rn(4, T, INTER)
         self.u = rn(5, T, INTER)
         self.y = rn(6, T, HIDDEN)
-        self.w = [rn(1000 * l + 7, HIDDEN, scale=0.1, loc=1.0) for l in range(layers)]
+        self.w = [rn(1000 * l + 7, HIDDEN, scale=0.1, loc=1.0, per_rank=False)
+                  for l in range(layers)]
         # RoPE tables for the rank's global positions (HF construction, fp32 -> bf16)
         pos = torch.arange(pos0, pos0 + T, device=device, dtype=torch.float32)
         inv = 1.0 / (THETA ** (torch.arange(0, HEAD, 2, device=device, dtype=torch.float32) / HEAD))
@@ -374,6 +376,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--eager-layers", type=int, default=4)
+    ap.add_argument("--no-op-configs", action="store_true")
     args = ap.parse_args()
     assert args.warmup >= 3 or os.environ.get("FL_B200_BENCH_ALLOW_SHORT"), "use --warmup >= 3"
 
@@ -413,8 +416,9 @@ def main():
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        # The rank's GPU is current; no device_id (torch_fl makes flagos the
+        # current accelerator, and NCCL binds to the current CUDA device).
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     T = args.tokens // world
     assert T * world == args.tokens, "tokens must split evenly across ranks"
     stack = Stack(T, args.layers, rank * T, dev, args.rounding, not args.no_fuse_add_norm)
@@ -424,7 +428,8 @@ def main():
         if world > 1:
             import torch.distributed as dist
 
-            dist.barrier()
+            # an all-reduce on the rank's own GPU: no device inference involved
+            dist.all_reduce(torch.zeros(1, device=dev))
         torch.cuda.synchronize()
 
     # warm-up
@@ -528,6 +533,12 @@ def main():
     # every rank checked on rank 0 against the oracle
     check = correctness_sample(stack, K, world, rank, dev)
 
+    per_op_configs = None
+    if world == 1 and not args.no_op_configs:
+        del stack.g, stack.u, stack.a        # room for the 17 GB softmax config
+        torch.cuda.empty_cache()
+        per_op_configs = op_configs(dev, measured_peak()[0])
+
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -547,7 +558,7 @@ def main():
                        "l2": "inputs larger than L2 (every per-rank activation >= 256 MB)"},
             "hbm_gbs_step": round(stack_bytes(stack) * args.steps / (ms / 1e3) / 1e9, 1),
             "per_op": per_op, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_eager_reference": eager,
+            "gpu_eager_reference": eager, "per_op_configs": per_op_configs,
             "gpu_launches": stack.launches_per_step() * args.steps,
             "clocks": clock_info, "correctness": check,
         }
@@ -556,6 +567,78 @@ def main():
         import torch.distributed as dist
 
         dist.destroy_process_group()
+
+
+def op_configs(dev, peak, reps=5):
+    """Per-op HBM GB/s on the other benchmark configurations (device time,
+    CUDA events, median of `reps` after 2 warm-ups; inputs resident, each
+    larger than L2 except the 67 MB RMSNorm f32 config, which is
+    launch-bound and reported for completeness)."""
+    from torch_fl import kernels as K
+
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(7)
+
+    def timed(name, fn, nbytes, note=""):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        ms = statistics.median(ts)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"ms": round(ms, 4), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                     "bytes": int(nbytes)}
+        if note:
+            out[name]["note"] = note
+
+    # config 1: RMSNorm fp32 [2048, 4096], eps 1e-6
+    x = torch.randn(2048, 4096, generator=g, device=dev)
+    w = 1 + 0.1 * torch.randn(4096, generator=g, device=dev)
+    timed("rms_norm_f32_2048x4096", lambda: K.rms_norm(x, w, 1e-6), 2 * x.numel() * 4 + 4096 * 4,
+          "67 MB: fits L2, launch-bound")
+    del x, w
+    # config 3: causal softmax
+    for dt, L, name in ((torch.bfloat16, 2048, "bf16_8x32x2048x2048"),
+                        (torch.float16, 4096, "f16_8x32x4096x4096")):
+        lg = (3.0 * torch.randn(8, 32, L, L, generator=g, device=dev)).to(dt)
+        masked = lg.masked_fill(torch.triu(torch.ones(L, L, dtype=torch.bool, device=dev), 1),
+                                float("-inf"))
+        n = lg.numel()
+        timed(f"softmax_{name}", lambda: K.softmax(masked), 4 * n, "pre-masked logits")
+        vis = 8 * 32 * L * (L + 1) // 2
+        timed(f"causal_softmax_{name}", lambda: K.softmax(lg, causal=True), 2 * vis + 2 * n,
+              "mask applied in the kernel; masked keys not read")
+        timed(f"softmax_{name}_f32_out", lambda: K.softmax(masked, out_dtype=torch.float32),
+              2 * n + 4 * n, "half_to_float (HF softmax(dtype=float32))")
+        del lg, masked
+    # config 4: reductions
+    xf = torch.randn(65536, 8192, generator=g, device=dev)
+    n = xf.numel()
+    timed("sum_lastdim_f32_65536x8192", lambda: K.sum_lastdim(xf), 4 * n + 4 * 65536)
+    timed("mean_lastdim_f32_65536x8192", lambda: K.mean_lastdim(xf), 4 * n + 4 * 65536)
+    timed("amax_lastdim_f32_65536x8192", lambda: K.amax_lastdim(xf), 4 * n + 4 * 65536)
+    timed("sum_all_f32_65536x8192", lambda: K.sum_all(xf), 4 * n + 4)
+    timed("mean_all_f32_65536x8192", lambda: K.mean_all(xf), 4 * n + 4)
+    timed("amax_all_f32_65536x8192", lambda: K.amax_all(xf), 4 * n + 4)
+    del xf
+    xa = torch.randn(65536, 32000, generator=g, device=dev).to(torch.bfloat16)
+    timed("argmax_lastdim_bf16_65536x32000", lambda: K.argmax_lastdim(xa),
+          2 * xa.numel() + 8 * 65536)
+    del xa
+    xi = torch.randint(-1000, 1001, (65536, 8192), generator=g, device=dev, dtype=torch.int32)
+    timed("sum_i32_i64_lastdim_65536x8192", lambda: K.sum_i32_i64(xi, False),
+          4 * xi.numel() + 8 * 65536)
+    timed("sum_i32_i64_all_65536x8192", lambda: K.sum_i32_i64(xi, True), 4 * xi.numel() + 8)
+    del xi
+    torch.cuda.empty_cache()
+    return out
 
 
 def stack_bytes(stack):

@@ -228,20 +228,25 @@ class Stack:
         self.fcos, self.fsin = v(self.cos), v(self.sin)
         self.fw = [v(w) for w in self.w]
 
-    def run_flagos(self, x):
+    def run_flagos(self, x, rows=None):
         """One step through torch_fl.ops (flagos:: ops through PyTorch's
-        dispatcher, outputs allocated by the flagos allocator)."""
+        dispatcher, outputs allocated by the flagos allocator) over the
+        tokens `rows` (a slice; all tokens when None).  Every op of the stack
+        is per token, so a token chunk runs the same 32 layers on its rows."""
         import torch_fl.ops as O
 
+        s = slice(None) if rows is None else rows
+        fq, fk, fg, fu, fy = self.fq[:, s], self.fk[:, s], self.fg[s], self.fu[s], self.fy[s]
+        fcos, fsin = self.fcos[s], self.fsin[s]
         r = self.rounding
         n = O.rms_norm(x, self.fw[0], EPS, r)
         for l in range(self.L):
-            qo, ko = O.rope_qk(self.fq, self.fk, self.fcos, self.fsin, 2, r)
+            qo, ko = O.rope_qk(fq, fk, fcos, fsin, 2, r)
             if l + 1 < self.L:
-                a = O.swiglu(self.fg, self.fu, r)
-                n, x = O.add_rms_norm(x, self.fy, self.fw[l + 1], EPS, r)
+                a = O.swiglu(fg, fu, r)
+                n, x = O.add_rms_norm(x, fy, self.fw[l + 1], EPS, r)
             else:
-                a, x = O.swiglu_residual(self.fg, self.fu, x, self.fy, r)
+                a, x = O.swiglu_residual(fg, fu, x, fy, r)
         return x
 
     def run_torch_eager(self, x, layers):
@@ -374,6 +379,9 @@ def main():
     ap.add_argument("--cpu-reps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-chunks", type=int, default=4,
+                    help="token chunks per e2e step: host->device copies, the layers and the "
+                         "device->host copies of different chunks overlap on three flagos streams")
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--eager-layers", type=int, default=4)
     ap.add_argument("--no-op-configs", action="store_true")
@@ -478,27 +486,62 @@ def main():
                 "traffic": traffic, "algorithmic_bytes": dom_bytes}
 
     # End to end through the reference-facing plugin API: the hidden state
-    # comes from pinned host memory into a flagos tensor, the 32 layers run as
+    # comes from pinned host memory into flagos tensors, the 32 layers run as
     # torch_fl.ops (flagos:: ops through PyTorch's dispatcher, outputs from
-    # the flagos allocator), the result goes back to host memory; all inside
-    # the timed region, on the flagos device's current stream.
+    # the flagos allocator), the result goes back to pinned host memory; all
+    # inside the timed region.  The step is cut into token chunks: chunk c's
+    # host->device copy (stream `h2d`), its layers (the current stream) and
+    # its device->host copy (stream `d2h`) are ordered by flagos events, so
+    # PCIe traffic in both directions overlaps the layers of other chunks.
     e2e = None
     if not args.no_e2e:
+        import torch_fl.flagos as flagos
+
         fdev = torch.device("flagos", local)
         stack.flagos_views()
         h_in = torch.empty(T, HIDDEN, dtype=torch.bfloat16, pin_memory=True)
         h_in.copy_(stack.x0)
         h_out = torch.empty_like(h_in, pin_memory=True)
-        for _ in range(2):
-            h_out.copy_(stack.run_flagos(h_in.to(fdev, non_blocking=True)), non_blocking=True)
+        chunks = max(1, min(args.e2e_chunks, T))
+        bounds = [(T * c // chunks, T * (c + 1) // chunks) for c in range(chunks)]
+        comp = flagos.current_stream(local)
+        h2d, d2h = flagos.Stream(local), flagos.Stream(local)
+        # At most two steps in flight: the host waits for step s-2's last
+        # device->host copy before queueing step s, as a serving loop bounds
+        # its queue (device memory then stays at two steps' buffers).
+        inflight = []
+
+        def e2e_step():
+            for lo, hi in bounds:
+                with flagos.stream(h2d):
+                    x_d = h_in[lo:hi].to(fdev, non_blocking=True)
+                    landed = flagos.Event()
+                    landed.record(h2d)
+                comp.wait_event(landed)
+                x_d.record_stream(comp)
+                res = stack.run_flagos(x_d, slice(lo, hi))
+                done = flagos.Event()
+                done.record(comp)
+                d2h.wait_event(done)
+                with flagos.stream(d2h):
+                    h_out[lo:hi].copy_(res, non_blocking=True)
+                res.record_stream(d2h)
+            ev = flagos.Event()
+            ev.record(d2h)
+            inflight.append(ev)
+            if len(inflight) > 2:
+                inflight.pop(0).synchronize()
+
+        for _ in range(max(args.warmup, 3)):
+            e2e_step()
+        comp.wait_stream(d2h)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
+        e0.record(comp)
         for _ in range(args.steps):
-            x_d = h_in.to(fdev, non_blocking=True)
-            res = stack.run_flagos(x_d)
-            h_out.copy_(res, non_blocking=True)
-        e1.record()
+            e2e_step()
+        comp.wait_stream(d2h)          # the last chunk is in host memory at e1
+        e1.record(comp)
         torch.cuda.synchronize()
         ems = sharding.max_over_ranks(e0.elapsed_time(e1), dev)
         # the e2e result equals the device-resident path's result
@@ -507,7 +550,9 @@ def main():
         e2e = {"value": args.tokens * args.steps / (ems / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": nbytes * world, "d2h_bytes_per_step": nbytes * world,
                "ms_per_step": ems / args.steps, "matches_device_path": same,
-               "api": "torch_fl.ops (flagos:: ops) on flagos tensors, host<->flagos copies"}
+               "chunks": chunks,
+               "api": "torch_fl.ops (flagos:: ops) on flagos tensors, host<->flagos copies "
+                      "on flagos streams overlapping the layers"}
 
     # PyTorch's own CUDA kernels on the HF formulas (the kernels the
     # reference's cuda route runs), same stack, `eager_layers` layers timed
@@ -572,8 +617,7 @@ def main():
 def op_configs(dev, peak, reps=5):
     """Per-op HBM GB/s on the other benchmark configurations (device time,
     CUDA events, median of `reps` after 2 warm-ups; inputs resident, each
-    larger than L2 except the 67 MB RMSNorm f32 config, which is
-    launch-bound and reported for completeness)."""
+    larger than L2 except the 67 MB RMSNorm f32 config, which L2 holds)."""
     from torch_fl import kernels as K
 
     out = {}
@@ -586,6 +630,9 @@ def op_configs(dev, peak, reps=5):
         ts = []
         for _ in range(reps):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            # A bounded spin kernel keeps the GPU busy while the host prepares
+            # the launch, so the events bracket the op's device time only.
+            torch.cuda._sleep(2_000_000)
             a.record()
             fn()
             b.record()
@@ -602,7 +649,7 @@ def op_configs(dev, peak, reps=5):
     x = torch.randn(2048, 4096, generator=g, device=dev)
     w = 1 + 0.1 * torch.randn(4096, generator=g, device=dev)
     timed("rms_norm_f32_2048x4096", lambda: K.rms_norm(x, w, 1e-6), 2 * x.numel() * 4 + 4096 * 4,
-          "67 MB: fits L2, launch-bound")
+          "67 MB: fits in L2")
     del x, w
     # config 3: causal softmax
     for dt, L, name in ((torch.bfloat16, 2048, "bf16_8x32x2048x2048"),

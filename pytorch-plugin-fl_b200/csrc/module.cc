@@ -92,6 +92,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     d["bytes_in_use"] = s.bytes_in_use;
     d["peak_bytes_in_use"] = s.peak_bytes_in_use;
     d["pool_reserved"] = s.pool_reserved;
+    d["pending_frees"] = s.pending_frees;
+    d["stream_uses"] = s.stream_uses;
     return d;
   });
   m.def("_empty_cache", &R::empty_cache);

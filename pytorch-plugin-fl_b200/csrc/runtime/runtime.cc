@@ -106,12 +106,14 @@ class PoolAllocator final : public c10::Allocator {
     if (nbytes == 0) return {nullptr, nullptr, &raw_delete, dev};
     const cudaStream_t s = current_stream(d);
     cudaMemPool_t pool = pool_for(d);
+    release_pending();
     void* p = nullptr;
     cudaError_t e = cudaMallocFromPoolAsync(&p, nbytes, pool, s);
     if (e == cudaErrorMemoryAllocation) {
       // Give cached memory back (ours and torch's CUDA cache) and retry once.
       (void)cudaGetLastError();
       C10_CUDA_CHECK(cudaDeviceSynchronize());
+      release_pending();  // this device's pending blocks are idle now
       C10_CUDA_CHECK(cudaMemPoolTrimTo(pool, 0));
       c10::cuda::CUDACachingAllocator::emptyCache();
       e = cudaMallocFromPoolAsync(&p, nbytes, pool, s);
@@ -153,6 +155,7 @@ class PoolAllocator final : public c10::Allocator {
     for (auto u : b.uses)
       if (u == s) return true;
     b.uses.push_back(s);
+    stream_uses_.fetch_add(1, std::memory_order_relaxed);
     return true;
   }
 
@@ -162,6 +165,11 @@ class PoolAllocator final : public c10::Allocator {
     st.frees = frees_.load();
     st.bytes_in_use = in_use_.load();
     st.peak_bytes_in_use = peak_.load();
+    st.stream_uses = stream_uses_.load();
+    {
+      std::lock_guard<std::mutex> lock(mu_);
+      st.pending_frees = pending_.size();
+    }
     for (int d = 0; d < kMaxDevices; ++d) {
       cudaMemPool_t pool = pools_[d].load();
       if (!pool) continue;
@@ -180,6 +188,7 @@ class PoolAllocator final : public c10::Allocator {
       if (!pool) continue;
       DeviceScope scope(d);
       C10_CUDA_CHECK(cudaDeviceSynchronize());
+      release_pending();
       C10_CUDA_CHECK(cudaMemPoolTrimTo(pool, 0));
     }
   }
@@ -198,20 +207,67 @@ class PoolAllocator final : public c10::Allocator {
       b = std::move(it->second);
       blocks_.erase(it);
     }
-    DeviceScope scope(b.device);
-    // The block may be reused by work on its allocation stream only after
-    // every other stream that used it has reached this point.
-    for (cudaStream_t u : b.uses) {
-      cudaEvent_t ev = nullptr;
-      if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) == cudaSuccess) {
-        (void)cudaEventRecord(ev, u);
-        (void)cudaStreamWaitEvent(b.stream, ev, 0);
-        (void)cudaEventDestroy(ev);  // released once the wait has been satisfied
-      }
-    }
-    if (cudaFreeAsync(p, b.stream) != cudaSuccess) (void)cudaGetLastError();
     frees_.fetch_add(1, std::memory_order_relaxed);
     in_use_.fetch_sub(b.size, std::memory_order_relaxed);
+    DeviceScope scope(b.device);
+    if (b.uses.empty()) {
+      // Stream-ordered: later work on the allocation stream may reuse it.
+      if (cudaFreeAsync(p, b.stream) != cudaSuccess) (void)cudaGetLastError();
+    } else {
+      // Other streams used the block: it goes back to the pool only once
+      // each of them has passed this point (an event per stream).  No
+      // stream waits for another here, so a copy stream can run ahead of
+      // the compute stream that reads its buffers.
+      Pending pend{p, b.device, b.stream, {}};
+      for (cudaStream_t u : b.uses) {
+        cudaEvent_t ev = nullptr;
+        if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
+          (void)cudaGetLastError();
+          // No event: fall back to ordering the allocation stream after u.
+          C10_CUDA_CHECK(cudaStreamSynchronize(u));
+          continue;
+        }
+        C10_CUDA_CHECK(cudaEventRecord(ev, u));
+        pend.events.push_back(ev);
+      }
+      std::lock_guard<std::mutex> lock(mu_);
+      pending_.push_back(std::move(pend));
+    }
+    release_pending();
+  }
+
+  // Frees the pending blocks whose streams have all passed their events.
+  void release_pending() {
+    std::vector<Pending> ready;
+    {
+      std::lock_guard<std::mutex> lock(mu_);
+      if (pending_.empty()) return;
+      size_t keep = 0;
+      for (size_t i = 0; i < pending_.size(); ++i) {
+        bool done = true;
+        for (cudaEvent_t ev : pending_[i].events) {
+          if (cudaEventQuery(ev) == cudaErrorNotReady) {
+            (void)cudaGetLastError();  // not an error: the stream is still busy
+            done = false;
+            break;
+          }
+        }
+        if (done) {
+          ready.push_back(std::move(pending_[i]));
+        } else {
+          // Never move an entry onto itself: a self-moved vector may come out
+          // empty, and an entry without events would be freed at once.
+          if (keep != i) pending_[keep] = std::move(pending_[i]);
+          ++keep;
+        }
+      }
+      pending_.resize(keep);
+    }
+    for (Pending& r : ready) {
+      DeviceScope scope(r.device);
+      for (cudaEvent_t ev : r.events) (void)cudaEventDestroy(ev);
+      if (cudaFreeAsync(r.ptr, r.stream) != cudaSuccess) (void)cudaGetLastError();
+    }
   }
 
   cudaMemPool_t pool_for(c10::DeviceIndex d) {
@@ -231,15 +287,33 @@ class PoolAllocator final : public c10::Allocator {
     // driver at every synchronisation.
     uint64_t keep = std::numeric_limits<uint64_t>::max();
     C10_CUDA_CHECK(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+    // A freed block is reused only by allocations on the stream that freed
+    // it (stream order makes that safe); cross-stream use is handled by
+    // record_stream and the deferred frees above.  The pool's own
+    // cross-stream reuse would also add waits between streams (a copy stream
+    // held back behind the compute stream) that nothing asked for.
+    int off = 0;
+    C10_CUDA_CHECK(cudaMemPoolSetAttribute(pool, cudaMemPoolReuseFollowEventDependencies, &off));
+    C10_CUDA_CHECK(cudaMemPoolSetAttribute(pool, cudaMemPoolReuseAllowOpportunistic, &off));
+    C10_CUDA_CHECK(cudaMemPoolSetAttribute(pool, cudaMemPoolReuseAllowInternalDependencies, &off));
     pools_[d].store(pool, std::memory_order_release);
     return pool;
   }
 
+  // A freed block still in use by other streams, with an event per stream.
+  struct Pending {
+    void* ptr;
+    c10::DeviceIndex device;
+    cudaStream_t stream;
+    std::vector<cudaEvent_t> events;
+  };
+
   std::mutex mu_;
   std::unordered_map<void*, Block> blocks_;
+  std::vector<Pending> pending_;
   std::mutex pool_mu_;
   std::atomic<cudaMemPool_t> pools_[kMaxDevices] = {};
-  std::atomic<uint64_t> allocations_{0}, frees_{0}, in_use_{0}, peak_{0};
+  std::atomic<uint64_t> allocations_{0}, frees_{0}, in_use_{0}, peak_{0}, stream_uses_{0};
 };
 
 // ================================================================ guard ====

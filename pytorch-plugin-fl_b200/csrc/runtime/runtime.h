@@ -49,6 +49,8 @@ struct AllocatorStats {
   uint64_t bytes_in_use;     // bytes currently held by live tensors
   uint64_t peak_bytes_in_use;
   uint64_t pool_reserved;    // bytes the pools hold from the driver
+  uint64_t pending_frees;    // freed blocks waiting for other streams to pass their events
+  uint64_t stream_uses;      // record_stream calls that added a stream to a block
 };
 AllocatorStats allocator_stats();
 // Returns cached, unused memory of every pool to the driver.

@@ -77,6 +77,33 @@ def test_streams_events_and_allocator():
     assert torch.flagos.memory_stats()["frees"] >= before["frees"] + 1
 
 
+def test_recorded_block_waits_for_the_other_stream():
+    """A block freed while another stream (recorded with record_stream) still
+    has work queued goes back to the pool only after that stream passes the
+    free: allocations in between get other memory, however many there are,
+    and no stream is made to wait for another."""
+    user = torch.flagos.Stream()
+    n = 1 << 20
+    x = torch.empty(n, device=DEV)
+    x_ptr = x.data_ptr()
+    with torch.flagos.stream(user):
+        torch.cuda._sleep(400_000_000)           # keeps `user` busy ~0.2 s (a bounded spin)
+    x.record_stream(user)
+    del x
+    assert torch.flagos.memory_stats()["pending_frees"] >= 1
+    held = []
+    for _ in range(4):                           # each allocation polls the pending frees
+        y = torch.empty(n, device=DEV)
+        assert y.data_ptr() != x_ptr
+        held.append(y)
+    assert not user.query()                      # the block was held while `user` ran
+    user.synchronize()
+    torch.flagos.synchronize()
+    del held
+    torch.empty(n, device=DEV)                   # polls again: the block is released
+    assert torch.flagos.memory_stats()["pending_frees"] == 0
+
+
 # ------------------------------------------------------- routed aten ops --
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_add_mul_match_cpu(dtype):

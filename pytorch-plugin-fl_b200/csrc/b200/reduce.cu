@@ -23,7 +23,11 @@ namespace {
 
 constexpr int kBlock = 256;
 constexpr int kUnroll = 4;
-constexpr int64_t kTargetCtas = 2048;   // CTAs a split reduction aims for
+// CTAs a split reduction aims for: 27 per SM of a 148-SM B200, so a long
+// row's chunks fill every SM to the same depth and the last wave is short
+// (2048 CTAs of 1 MB left a 0.3-wave tail: 5.4 vs 6.8 TB/s row-wise).  The
+// parts of one row then fit the 64 KB scratch of the no-allocation sum.
+constexpr int64_t kTargetCtas = 148 * 27;
 constexpr int64_t kMinChunk = 16384;    // elements per CTA before splitting pays
 constexpr int64_t kSplitRowsBelow = 1024;
 
@@ -106,6 +110,82 @@ __device__ __forceinline__ float elem_value(T v) {
   return Elem<T>::to_f(v);
 }
 
+// NaN-propagating max of a 16-byte pack (PTX max.NaN on packed pairs: one
+// instruction per two 16-bit elements), as fp32.  NaN if any element is NaN.
+__device__ __forceinline__ float max_nan_f32(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t max_nan_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t max_nan_f16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ float pack_max_nan(const uint4& u) {
+  if constexpr (std::is_same<T, float>::value) {
+    return max_nan_f32(max_nan_f32(__uint_as_float(u.x), __uint_as_float(u.y)),
+                       max_nan_f32(__uint_as_float(u.z), __uint_as_float(u.w)));
+  } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const uint32_t m = max_nan_bf16x2(max_nan_bf16x2(u.x, u.y), max_nan_bf16x2(u.z, u.w));
+    return max_nan_f32(__uint_as_float(m << 16), __uint_as_float(m & 0xffff0000u));
+  } else {
+    const uint32_t m = max_nan_f16x2(max_nan_f16x2(u.x, u.y), max_nan_f16x2(u.z, u.w));
+    const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&m));
+    return max_nan_f32(v.x, v.y);
+  }
+}
+
+// argmax of one thread's packs of a row chunk: packs p0 + t, p0 + t + kBlock,
+// ... below p1.  The loop keeps only the running max (fp32, NaN-propagating)
+// and the ordinal of the pack where it last rose: it rises where a pack's
+// max is larger, or NaN while the running max is a number; an equal value
+// never moves it (packs arrive in increasing index order, so the first stays).
+// Afterwards the winning pack is read again (from L2) and searched for its
+// first element equal to the max (or first NaN).  Same result as folding
+// element by element with first-index ties and NaN as the maximum.
+template <typename T, int U>
+__device__ __forceinline__ ArgMaxAcc argmax_packs(const T* xr, int64_t p0, int64_t p1) {
+  constexpr int VW = Elem<T>::kVec;
+  const int64_t first = p0 + threadIdx.x;
+  if (first >= p1) return ArgMaxPolicy::init();
+  const int n = (int)ceil_div(p1 - first, kBlock);   // this thread's packs
+  const T* base = xr + first * VW;
+  float best = -INFINITY;
+  int bestk = 0;  // a thread whose packs are all -inf keeps its first pack
+  for (int k0 = 0; k0 < n; k0 += U) {
+    const T* pk = base + (int64_t)k0 * kBlock * VW;
+    uint4 v[U];
+#pragma unroll
+    for (int k = 0; k < U; ++k)
+      if (k0 + k < n) v[k] = ld_stream(pk + k * kBlock * VW);
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      if (k0 + k < n) {
+        const float nb = max_nan_f32(best, pack_max_nan<T>(v[k]));
+        const bool rose = (nb != best) && (best == best);
+        bestk = rose ? k0 + k : bestk;
+        best = nb;
+      }
+    }
+  }
+  const uint4 w = ld_stream(base + (int64_t)bestk * kBlock * VW);
+  float f[VW];
+  unpack<T>(w, f);
+  const bool nan = best != best;
+  int e = VW - 1;
+#pragma unroll
+  for (int k = VW - 1; k >= 0; --k)
+    if (nan ? f[k] != f[k] : f[k] == best) e = k;
+  return ArgMaxAcc{best, (long long)((first + (int64_t)bestk * kBlock) * VW + e)};
+}
+
 template <typename T, typename P>
 __device__ __forceinline__ void fold_pack(typename P::Acc& acc, const uint4& u, int64_t j0) {
   if constexpr (std::is_same<T, int32_t>::value) {
@@ -160,6 +240,37 @@ __device__ __forceinline__ typename P::Acc block_merge(typename P::Acc a) {
   return a;
 }
 
+// The cross-CTA partials of a policy seen as a policy of their own, so the
+// last CTA of a split row merges them with block_merge.
+template <typename T>
+__device__ __forceinline__ T shfl_part(T a, int off) {
+  return __shfl_xor_sync(0xffffffffu, a, off);
+}
+template <>
+__device__ __forceinline__ ArgMaxAcc shfl_part<ArgMaxAcc>(ArgMaxAcc a, int off) {
+  return ArgMaxPolicy::shfl(a, off);
+}
+template <typename P>
+struct PartOps {
+  using Acc = typename P::Part;
+  __device__ static Acc shfl(Acc a, int off) { return shfl_part(a, off); }
+  __device__ static Acc merge(Acc a, Acc b) { return P::pmerge(a, b); }
+};
+
+// A partial written by another CTA of the grid (read past L1).
+template <typename Part>
+__device__ __forceinline__ Part load_part(const Part* p) {
+  const volatile Part* v = p;
+  if constexpr (std::is_same<Part, ArgMaxAcc>::value) {
+    Part r;
+    r.v = v->v;
+    r.i = v->i;
+    return r;
+  } else {
+    return *v;
+  }
+}
+
 // ---- final stores -----------------------------------------------------------
 enum Final { kFinalSum = 0, kFinalMean = 1, kFinalMax = 2, kFinalIdx = 3, kFinalI64 = 4 };
 
@@ -210,17 +321,24 @@ reduce_rows_kernel(const T* x, int64_t ld, int64_t rows, int64_t cols, int64_t s
     const T* xr = x + r * ld;
     Acc acc = P::init();
     if (VEC) {
-      // chunk and ld are multiples of VW, so every pack is whole.
+      // chunk and ld are multiples of VW, so every pack is whole.  Loads go
+      // out in batches of kUnroll packs per thread, the row's ragged end
+      // included (a predicated batch), so a thread waits for HBM once per
+      // batch.
       const int64_t p0 = c0 / VW, p1 = c1 / VW;
-      int64_t p = p0 + threadIdx.x;
-      for (; p + (kUnroll - 1) * kBlock < p1; p += kUnroll * kBlock) {
-        uint4 v[kUnroll];
+      if constexpr (std::is_same<P, ArgMaxPolicy>::value && !std::is_integral<T>::value) {
+        acc = argmax_packs<T, 8>(xr, p0, p1);
+      } else {
+        for (int64_t p = p0 + threadIdx.x; p < p1; p += kUnroll * kBlock) {
+          uint4 v[kUnroll];
 #pragma unroll
-        for (int k = 0; k < kUnroll; ++k) v[k] = ld_stream(xr + (p + k * kBlock) * VW);
+          for (int k = 0; k < kUnroll; ++k)
+            if (p + k * kBlock < p1) v[k] = ld_stream(xr + (p + k * kBlock) * VW);
 #pragma unroll
-        for (int k = 0; k < kUnroll; ++k) fold_pack<T, P>(acc, v[k], (p + k * kBlock) * VW);
+          for (int k = 0; k < kUnroll; ++k)
+            if (p + k * kBlock < p1) fold_pack<T, P>(acc, v[k], (p + k * kBlock) * VW);
+        }
       }
-      for (; p < p1; p += kBlock) fold_pack<T, P>(acc, ld_stream(xr + p * VW), p * VW);
     } else {
       for (int64_t c = c0 + threadIdx.x; c < c1; c += kBlock) fold_scalar<T, P>(acc, xr + c, c);
     }
@@ -237,21 +355,16 @@ reduce_rows_kernel(const T* x, int64_t ld, int64_t rows, int64_t cols, int64_t s
     }
     __syncthreads();
     if (last) {
-      // Every other CTA of this row has published its partial.
+      // Every other CTA of this row has published its partial.  Thread t
+      // merges partials t, t + kBlock, ... in order, then the CTA merges the
+      // threads in a fixed tree: the result does not depend on CTA timing.
       __threadfence();
+      const Part* pr = parts + r * splits;
+      Part acc2 = P::pinit();
+      for (int64_t k = threadIdx.x; k < splits; k += kBlock)
+        acc2 = P::pmerge(acc2, load_part(pr + k));
+      acc2 = block_merge<PartOps<P>>(acc2);
       if (threadIdx.x == 0) {
-        Part acc2 = P::pinit();
-        const volatile Part* pr = parts + r * splits;
-        for (int64_t k = 0; k < splits; ++k) {
-          Part pk;
-          if constexpr (std::is_same<Part, ArgMaxAcc>::value) {
-            pk.v = pr[k].v;
-            pk.i = pr[k].i;
-          } else {
-            pk = pr[k];
-          }
-          acc2 = P::pmerge(acc2, pk);
-        }
         store_final_part<P, FINAL>(out, r, out_dtype, acc2, cols);
         tickets[r] = 0u;  // leave the workspace ready for the next call
       }

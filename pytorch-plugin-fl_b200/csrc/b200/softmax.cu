@@ -15,8 +15,58 @@ namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// 2^t with the PTX instruction ex2.approx.ftz.f32 (relative error about
+// 2^-22 over the fp32 normal range; results below it flush to +0, inputs
+// -inf -> +0, NaN -> NaN).
+__device__ __forceinline__ float ex2_approx(float t) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(t));
+  return r;
+}
+
+// exp(x - m) as 2^(x*log2e - m*log2e), one FMA and one ex2.
 __device__ __forceinline__ float exp_shifted(float x, float mlog2e) {
-  return exp2f(fmaf(x, kLog2e, -mlog2e));
+  return ex2_approx(fmaf(x, kLog2e, -mlog2e));
+}
+
+// Max of a 16-byte pack as fp32, NaN ignored like fmaxf (a NaN anywhere in
+// the row still makes every output NaN through its exp).  16-bit packs use
+// the packed max.bf16x2 / max.f16x2 instructions: 3 for 8 elements.
+template <typename T>
+__device__ __forceinline__ float pack_max(const uint4& u) {
+  if constexpr (std::is_same<T, float>::value) {
+    return fmaxf(fmaxf(__uint_as_float(u.x), __uint_as_float(u.y)),
+                 fmaxf(__uint_as_float(u.z), __uint_as_float(u.w)));
+  } else {
+    uint32_t a, b, m;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      asm("max.bf16x2 %0, %1, %2;" : "=r"(a) : "r"(u.x), "r"(u.y));
+      asm("max.bf16x2 %0, %1, %2;" : "=r"(b) : "r"(u.z), "r"(u.w));
+      asm("max.bf16x2 %0, %1, %2;" : "=r"(m) : "r"(a), "r"(b));
+      return fmaxf(__uint_as_float(m << 16), __uint_as_float(m & 0xffff0000u));
+    } else {
+      asm("max.f16x2 %0, %1, %2;" : "=r"(a) : "r"(u.x), "r"(u.y));
+      asm("max.f16x2 %0, %1, %2;" : "=r"(b) : "r"(u.z), "r"(u.w));
+      asm("max.f16x2 %0, %1, %2;" : "=r"(m) : "r"(a), "r"(b));
+      const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&m));
+      return fmaxf(v.x, v.y);
+    }
+  }
+}
+
+// Calls f(integral_constant<int, k>) for the runtime count k in [N, MAX]: a
+// chain of compares on a value uniform over a row's threads, so a causal
+// row runs code for its visible pack iterations only, with every register
+// array still indexed by constants.
+template <int N, int MAX, typename F>
+__device__ __forceinline__ void with_count(int k, F& f) {
+  if constexpr (N <= MAX) {
+    if (k == N) {
+      f(std::integral_constant<int, N>{});
+      return;
+    }
+    with_count<N + 1, MAX>(k, f);
+  }
 }
 
 // Stores VW fp32 values (one input pack's worth) as TO at `o`.
@@ -63,11 +113,22 @@ __device__ __forceinline__ uint4 mask_tail<__half>(uint4 v, int keep) {
   return mask_tail16<0xfc00>(v, keep);
 }
 
+// Resident CTAs per SM the register budget is set for.  A causal row reads
+// only its visible keys, so each row has fewer bytes in flight than a plain
+// one; causal rows therefore keep no fp32 exps in registers (they evaluate
+// exp again when storing: one ex2 per element on average, since about half
+// the keys are masked) and run twice as many rows per SM (<= 64 registers at
+// 256 threads).
+template <int BLOCK, bool CAUSAL>
+constexpr int softmax_min_blocks() {
+  return CAUSAL ? (BLOCK <= 256 ? 4 : 1024 / BLOCK) : ladder_min_blocks<BLOCK>();
+}
+
 // Masked keys are loaded as -inf, so the max ignores them, their exp is an
 // exact 0 and a row with no visible key comes out NaN (-inf - -inf), with no
 // per-element masks in the arithmetic.
 template <typename TI, typename TO, int TPR, int VPT, int BLOCK, bool CAUSAL>
-__global__ void __launch_bounds__(BLOCK, ladder_min_blocks<BLOCK>())
+__global__ void __launch_bounds__(BLOCK, (softmax_min_blocks<BLOCK, CAUSAL>()))
 softmax_vec_kernel(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
                    int64_t cols, int64_t q_len, int64_t offset) {
   constexpr int VW = Elem<TI>::kVec;
@@ -84,48 +145,93 @@ softmax_vec_kernel(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
     int nvalid = (int)cols;
     if (CAUSAL) nvalid = (int)max((int64_t)0, min(cols, (row % q_len) + offset + 1));
     const TI* xr = x + row * ldx;
+    // Pack iterations i >= `iters` lie wholly past a causal row's last
+    // visible key for every thread of the row: they are neither loaded nor
+    // computed, and store zeros.  Inside the visible iterations a thread
+    // whose pack is masked holds -inf (exp 0).  The phases run through
+    // with_count, so this costs no predicated-off work; the reductions stay
+    // outside it, where every thread of the CTA reaches them.
+    const int iters =
+        CAUSAL ? (int)min((int64_t)VPT, ceil_div(ceil_div((int64_t)nvalid, VW), TPR)) : VPT;
     uint4 v[VPT];
+    float ex[VPT][VW];
+    float m = -INFINITY, s = 0.f;
+    auto load_max = [&](auto kc) {
+      constexpr int K = decltype(kc)::value;
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int j0 = (lane + i * TPR) * VW;
-      if (ok && j0 < nvalid) {
-        v[i] = ld_stream(xr + j0);
-        if (CAUSAL && j0 + VW > nvalid) v[i] = mask_tail<TI>(v[i], nvalid - j0);
-      } else {
-        v[i] = mask_tail<TI>(make_uint4(0, 0, 0, 0), 0);
+      for (int i = 0; i < K; ++i) {
+        const int j0 = (lane + i * TPR) * VW;
+        if (ok && j0 < nvalid) {
+          v[i] = ld_stream(xr + j0);
+          if (CAUSAL && j0 + VW > nvalid) v[i] = mask_tail<TI>(v[i], nvalid - j0);
+        } else {
+          v[i] = mask_tail<TI>(make_uint4(0, 0, 0, 0), 0);
+        }
       }
-    }
-    float m = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      float f[VW];
-      unpack<TI>(v[i], f);
+      for (int i = 0; i < K; ++i) m = fmaxf(m, pack_max<TI>(v[i]));
+    };
+    // exp(x - m) per element, each pack summed as a tree; plain rows keep the
+    // exps in fp32 registers for the store pass (one ex2 per element).
+    const auto exp_sum = [&](auto kc) {
+      constexpr int K = decltype(kc)::value;
+      const float ml = m * kLog2e;
 #pragma unroll
-      for (int e = 0; e < VW; ++e) m = fmaxf(m, f[e]);
-    }
-    m = row_reduce<FastMaxOp, TPR, BLOCK>(m, smem);
-    const float ml = m * kLog2e;
-    float s = 0.f;
+      for (int i = 0; i < K; ++i) {
+        float f[VW], t[VW];
+        unpack<TI>(opaque(v[i]), f);
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      float f[VW];
-      unpack<TI>(opaque(v[i]), f);
+        for (int e = 0; e < VW; ++e) t[e] = exp_shifted(f[e], ml);
+        if constexpr (!CAUSAL) {
 #pragma unroll
-      for (int e = 0; e < VW; ++e) s += exp_shifted(f[e], ml);
-    }
-    s = row_reduce<SumOp, TPR, BLOCK>(s, smem);
-    const float inv = 1.0f / s;
+          for (int e = 0; e < VW; ++e) ex[i][e] = t[e];
+        }
+#pragma unroll
+        for (int w = VW / 2; w >= 1; w /= 2)
+#pragma unroll
+          for (int e = 0; e < w; ++e) t[e] += t[e + w];
+        s += t[0];
+      }
+    };
     TO* yr = y + row * ldy;
+    const auto store = [&](auto kc) {
+      constexpr int K = decltype(kc)::value;
+      const float inv = 1.0f / s;
+      const float ml = m * kLog2e;
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int vi = lane + i * TPR;
-      if (!ok || vi >= nvec) continue;
-      float f[VW], o[VW];
-      unpack<TI>(opaque(v[i]), f);
+      for (int i = 0; i < K; ++i) {
+        const int vi = lane + i * TPR;
+        if (!ok || vi >= nvec) continue;
+        float o[VW];
+        if constexpr (CAUSAL) {
+          unpack<TI>(opaque(v[i]), o);
 #pragma unroll
-      for (int e = 0; e < VW; ++e) o[e] = exp_shifted(f[e], ml) * inv;
-      store_vals<TO, VW>(yr + (int64_t)vi * VW, o);
-    }
+          for (int e = 0; e < VW; ++e) o[e] = exp_shifted(o[e], ml) * inv;
+        } else {
+#pragma unroll
+          for (int e = 0; e < VW; ++e) o[e] = ex[i][e] * inv;
+        }
+        store_vals<TO, VW>(yr + (int64_t)vi * VW, o);
+      }
+      // Masked keys: exp = 0, so 0 * inv (NaN for a row with no visible key).
+      float z[VW];
+#pragma unroll
+      for (int e = 0; e < VW; ++e) z[e] = 0.f * inv;
+#pragma unroll
+      for (int i = K; i < VPT; ++i) {
+        const int vi = lane + i * TPR;
+        if (ok && vi < nvec) store_vals<TO, VW>(yr + (int64_t)vi * VW, z);
+      }
+    };
+    using Full = std::integral_constant<int, VPT>;
+    if constexpr (CAUSAL) with_count<0, VPT>(iters, load_max);
+    else load_max(Full{});
+    m = row_reduce<FastMaxOp, TPR, BLOCK>(m, smem);
+    if constexpr (CAUSAL) with_count<0, VPT>(iters, exp_sum);
+    else exp_sum(Full{});
+    s = row_reduce<SumOp, TPR, BLOCK>(s, smem);
+    if constexpr (CAUSAL) with_count<0, VPT>(iters, store);
+    else store(Full{});
   }
 }
 

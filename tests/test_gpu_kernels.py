@@ -377,6 +377,29 @@ def test_causal_softmax(L, offset):
         assert torch.isnan(got[..., 0, :]).all()
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("cols", [512, 1024, 2048, 4096, 8192, 16384])
+def test_softmax_row_rungs(dtype, cols):
+    """Every rung of the register-row ladder from 512 to 16384 keys (4..128
+    threads per row, up to 8 packs per thread, and the looped kernel beyond),
+    a ragged last group of rows, causal rows with a partly visible last pack
+    and a history offset (the causal kernel runs only its visible pack
+    iterations), fp32 output, and rows with a leading stride."""
+    dt = parity.dname(dtype)
+    x = rnd((37, cols), dtype, 50 + cols, scale=3.0)
+    check_float(K.softmax(x), ops.softmax_golden(parity.to_np(x), dt), dt, f"plain {cols}")
+    wide = rnd((37, cols + 64), dtype, 51 + cols, scale=3.0)[:, :cols]   # ld = cols + 64
+    check_float(K.softmax(wide), ops.softmax_golden(parity.to_np(wide), dt), dt, f"strided {cols}")
+    if dtype != torch.float32:
+        parity.assert_rel(parity.to_np(K.softmax(x, out_dtype=torch.float32)),
+                          ops.softmax_golden(parity.to_np(x), "f32"), rtol=1e-5, atol=1e-30)
+    xc = rnd((2, 19, cols), dtype, 52 + cols, scale=3.0)
+    for off in (cols // 3 + 1, cols - 19):
+        got = K.softmax(xc, causal=True, causal_offset=off)
+        ref = ops.softmax_golden(parity.to_np(xc), dt, causal=True, offset=off)
+        check_float(got, ref, dt, f"causal {cols} off={off}")
+
+
 def test_softmax_infinities():
     x = torch.tensor([[float("-inf")] * 8, [0.0, float("-inf"), 1.0, float("-inf"), 2, 3, 4, 5],
                       [1.0, float("nan"), 2, 3, 4, 5, 6, 7], [float("inf"), 1, 2, 3, 4, 5, 6, 7]])
@@ -481,6 +504,27 @@ def test_argmax_ties_nan_split(cols):
     got = K.argmax_lastdim(x.to(DEV)).cpu().numpy()
     parity.assert_exact(got, native.argmax_rows_bf16(x.view(torch.int16).numpy().view(np.uint16)), "C oracle")
     parity.assert_exact(got, x.argmax(-1).numpy(), "torch CPU")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("cols", [8, 37, 4096, 100_003])
+def test_argmax_dense_ties_all_dtypes(dtype, cols):
+    """Ties inside one 16-byte pack and across packs, +-0, NaN and inf
+    mixes: the kernel folds whole packs (packed max, then a search of the
+    winning pack), and must still return the first index of the maximum."""
+    g = torch.Generator().manual_seed(41 + cols)
+    x = torch.randint(-3, 4, (7, cols), generator=g).to(dtype)   # many exact ties
+    x[1] = 0.0
+    x[1, : cols // 2] = -0.0                 # -0 == +0: the first zero wins
+    x[2, cols // 3] = float("nan")
+    x[3] = float("-inf")
+    x[4, 1::3] = float("inf")
+    x[4, cols - 1] = float("nan")            # NaN beats inf
+    x[5, cols - 1] = 3.5                     # the max in the last element
+    x[6] = -1.0
+    x[6, cols // 2] = float("-inf")
+    got = K.argmax_lastdim(x.to(DEV)).cpu()
+    assert torch.equal(got, x.argmax(-1)), (got, x.argmax(-1))
 
 
 def test_sum_i32_full_size_exact():

@@ -23,7 +23,7 @@ from torch_fl import _abi
 pytestmark = pytest.mark.gpu
 
 CASES = [
-    (50_000_000, torch.float32),   # split over 2048 CTAs: the scratch is used
+    (50_000_000, torch.float32),   # split over ~3000 CTAs: the scratch is used
     (3_000_001, torch.bfloat16),   # split, odd length, 16-bit input
     (1_000, torch.float32),        # single CTA: no scratch needed
 ]

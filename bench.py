@@ -385,7 +385,12 @@ def main():
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--eager-layers", type=int, default=4)
     ap.add_argument("--no-op-configs", action="store_true")
+    ap.add_argument("--profile-case", choices=sorted(PROFILE_CASES),
+                    help="run one small case of one op once on GPU 0 and exit (for ncu)")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     assert args.warmup >= 3 or os.environ.get("FL_B200_BENCH_ALLOW_SHORT"), "use --warmup >= 3"
 
     world = _env_int("WORLD_SIZE", 1)
@@ -695,6 +700,47 @@ def stack_bytes(stack):
         per = BYTES["rope_qk"] + BYTES["swiglu"]
         return T * (L * per + BYTES["rms_norm"] + (L - 1) * 4 * HIDDEN * BF16 + BYTES["residual_add"])
     return T * L * BYTES_PER_TOKEN_LAYER
+
+
+# Small cases for ncu captures: each input larger than L2 (126 MB) and a few
+# GB on the device at most; one launch of the op (after one warm-up launch).
+PROFILE_CASES = {
+    "stack": "2 layers of the stack on 16384 tokens (RMSNorm, RoPE, SwiGLU, add+RMSNorm, "
+             "RoPE, SwiGLU+residual); warm-up step first",
+    "softmax": "softmax bf16 [2, 32, 2048, 2048]",
+    "causal_softmax": "causal softmax bf16 [2, 32, 2048, 2048]",
+    "softmax_f16": "softmax f16 [1, 32, 4096, 4096]",
+    "argmax": "argmax bf16 [8192, 32000]",
+    "sum_all": "full sum f32 [16384, 8192]",
+}
+
+
+def profile_case(name):
+    from torch_fl import kernels as K
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(11)
+    if name == "stack":
+        st = Stack(16384, 2, 0, dev, "fused", True)
+        fn = lambda: st.run(st.x0)  # noqa: E731
+    elif name in ("softmax", "causal_softmax"):
+        x = (3.0 * torch.randn(2, 32, 2048, 2048, generator=g, device=dev)).to(torch.bfloat16)
+        fn = lambda: K.softmax(x, causal=name == "causal_softmax")  # noqa: E731
+    elif name == "softmax_f16":
+        x = (3.0 * torch.randn(1, 32, 4096, 4096, generator=g, device=dev)).to(torch.float16)
+        fn = lambda: K.softmax(x)  # noqa: E731
+    elif name == "argmax":
+        x = torch.randn(8192, 32000, generator=g, device=dev).to(torch.bfloat16)
+        fn = lambda: K.argmax_lastdim(x)  # noqa: E731
+    else:
+        x = torch.randn(16384, 8192, generator=g, device=dev)
+        fn = lambda: K.sum_all(x)  # noqa: E731
+    fn()
+    torch.cuda.synchronize()
+    fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": name, "what": PROFILE_CASES[name]}))
 
 
 def correctness_sample(stack, K, world, rank, dev):

@@ -93,18 +93,54 @@ def committed_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples during the timed region."""
+    """SM clock and clock-event reasons of one GPU, sampled during the timed
+    region: NVML polled from a thread every 10 ms (read-only queries), so a
+    timed region of ~0.1 s still gets samples; nvidia-smi every 200 ms when
+    NVML is unavailable."""
 
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index):
-        self.gpu = gpu_index
+        # NVML and nvidia-smi number GPUs physically; map through CUDA_VISIBLE_DEVICES.
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        self.gpu = int(ids[gpu_index]) if gpu_index < len(ids) and ids[gpu_index].isdigit() \
+            else gpu_index
+        self.samples = []
+        self.thread = None
         self.proc = None
         self.path = os.path.join("/tmp", f"fl_b200_clocks_{os.getpid()}.csv")
 
     def start(self):
+        try:
+            import threading
+
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            smax = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            masks = [(n, getattr(pynvml, c)) for n, c in self.REASONS]
+            self.stop_flag = threading.Event()
+
+            def poll():
+                while not self.stop_flag.is_set():
+                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((sm, smax, [n for n, m in masks if bits & m]))
+                    self.stop_flag.wait(0.01)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
@@ -114,6 +150,15 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+            if not self.samples:
+                return None
+            sm = [s[0] for s in self.samples]
+            reasons = sorted({r for s in self.samples for r in s[2]})
+            return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(s[1] for s in self.samples),
+                    "reasons": reasons, "samples": len(self.samples), "source": "nvml 10 ms"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -140,7 +185,7 @@ class ClockSampler:
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi 200 ms"}
 
 
 # ---------------------------------------------------------------- the stack
@@ -689,6 +734,26 @@ def op_configs(dev, peak, reps=5):
           4 * xi.numel() + 8 * 65536)
     timed("sum_i32_i64_all_65536x8192", lambda: K.sum_i32_i64(xi, True), 4 * xi.numel() + 8)
     del xi
+    # backward kernels (training through the path): bytes = inputs read once
+    # + outputs written once
+    xb = torch.randn(65536, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+    dyb = torch.randn(65536, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+    wb = (1 + 0.1 * torch.randn(HIDDEN, generator=g, device=dev)).to(torch.bfloat16)
+    timed("rms_norm_backward_bf16_65536x4096", lambda: K.rms_norm_backward(dyb, xb, wb, EPS),
+          3 * xb.numel() * BF16 + 2 * HIDDEN * BF16, "x, dy in; dx, dw out")
+    del xb, dyb
+    gb = torch.randn(16384, INTER, generator=g, device=dev).to(torch.bfloat16)
+    ub = torch.randn(16384, INTER, generator=g, device=dev).to(torch.bfloat16)
+    db = torch.randn(16384, INTER, generator=g, device=dev).to(torch.bfloat16)
+    timed("swiglu_backward_bf16_16384x14336", lambda: K.swiglu_backward(db, gb, ub),
+          5 * gb.numel() * BF16, "dout, gate, up in; dgate, dup out")
+    del gb, ub, db
+    lg = (3.0 * torch.randn(8, 32, 2048, 2048, generator=g, device=dev)).to(torch.bfloat16)
+    yb = K.softmax(lg, causal=True)
+    dyb = torch.randn(8, 32, 2048, 2048, generator=g, device=dev).to(torch.bfloat16)
+    timed("softmax_backward_bf16_8x32x2048x2048", lambda: K.softmax_backward(dyb, yb),
+          3 * yb.numel() * BF16, "dy, y in; dx out")
+    del lg, yb, dyb
     torch.cuda.empty_cache()
     return out
 

@@ -267,9 +267,9 @@ FL_B200_API int fl_b200_sum_i32_i64(const int32_t* x, int64_t ld, int64_t rows,
  * cross-CTA partials live in a fixed scratch array of                      *
  * FL_B200_NOALLOC_SCRATCH_BYTES inside this library: every GPU that loads  *
  * the library holds that array until the process exits.  A full-tensor    *
- * sum splits into at most 2048 partials (32 KiB); a request whose split    *
- * would not fit the scratch is rejected with FL_B200_ERR_TOO_LARGE before  *
- * anything is launched.                                                    *
+ * sum splits into at most 148*27 = 3996 partials of 16 bytes plus a 4-byte *
+ * ticket (63,940 bytes); a request whose split would not fit the scratch   *
+ * is rejected with FL_B200_ERR_TOO_LARGE before anything is launched.      *
  * The first call on a device looks up the scratch's device address        *
  * (cudaGetSymbolAddress) and caches it; make that first call before any    *
  * stream capture.  Every call shares the one scratch array, which keeps    *
@@ -281,6 +281,49 @@ FL_B200_API int fl_b200_sum_i32_i64(const int32_t* x, int64_t ld, int64_t rows,
 FL_B200_API int fl_b200_reduce_sum_all_noalloc(const void* x, int64_t n, void* out,
                                                int in_dtype, int out_dtype,
                                                fl_b200_stream_t stream);
+
+/* ------------------------------------------------------------------------ *
+ * Backward kernels (training through the fused ops).  fp32 math, one       *
+ * rounding to the output dtype.                                            *
+ *                                                                           *
+ * RMSNorm backward for out = w * x * r, r = 1/sqrt(mean(x^2) + eps):       *
+ *   dx = r * (w*dy - n * mean(w*dy*n)), n = x*r;  dw = sum over rows dy*n.  *
+ * Replaces autograd over the HF chain (modeling_qwen3.py:59-64), which the *
+ * reference runs as the backward of pow (pow.cu), mean, add, rsqrt, mul    *
+ * and the casts, op by op.  dw may be NULL (no weight gradient); else the  *
+ * call needs a device workspace of fl_b200_rms_norm_bwd_workspace_size     *
+ * bytes (per-CTA fp32 partials of dw, added in a fixed order: the result   *
+ * is deterministic).  The size depends on the current device's SM count.  */
+FL_B200_API size_t fl_b200_rms_norm_bwd_workspace_size(int64_t rows, int64_t cols);
+FL_B200_API int fl_b200_rms_norm_bwd(const void* dy, int64_t ld_dy, const void* x,
+                                     int64_t ld_x, const void* w, void* dx, int64_t ld_dx,
+                                     void* dw, int64_t rows, int64_t cols, float eps,
+                                     int dtype, void* workspace, size_t workspace_bytes,
+                                     fl_b200_stream_t stream);
+
+/* SwiGLU backward for out = silu(gate) * up over n dense elements:         *
+ *   dup = dout * silu(gate),  dgate = dout * up * s * (1 + gate*(1 - s)),   *
+ *   s = sigmoid(gate).                                                      *
+ * Replaces silu_backward (csrc/aten/register.cc:329-331 -> csrc/aten/      *
+ * backends/cuda/silu_backward.cu:15-35) plus the two mul.Tensor backward   *
+ * products (mul.cu:28-52).                                                 */
+FL_B200_API int fl_b200_swiglu_bwd(const void* dout, const void* gate, const void* up,
+                                   void* dgate, void* dup, int64_t n, int dtype,
+                                   fl_b200_stream_t stream);
+/* silu_backward over n dense elements: dx = dout * s * (1 + x*(1 - s)).     *
+ * Replaces silu_backward.cu:15-35 (same formula, fp32 op math).            */
+FL_B200_API int fl_b200_silu_bwd(const void* dout, const void* x, void* dx, int64_t n,
+                                 int dtype, fl_b200_stream_t stream);
+
+/* Softmax backward over the last dim: dx = y * (dy - sum(dy * y)).          *
+ * dy and y share in_dtype; out_dtype = in_dtype, or BF16/F16 with F32       *
+ * inputs (the backward of a half_to_float softmax).  Replaces              *
+ * _softmax_backward_data, which the reference leaves unregistered (CPU      *
+ * fallback, csrc/aten/register.cc:439-442 -> fallback.cc:12-14).           */
+FL_B200_API int fl_b200_softmax_bwd(const void* dy, int64_t ld_dy, const void* y,
+                                    int64_t ld_y, void* dx, int64_t ld_dx, int64_t rows,
+                                    int64_t cols, int in_dtype, int out_dtype,
+                                    fl_b200_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

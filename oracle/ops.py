@@ -269,3 +269,91 @@ def sum_i32_i64(x, axis=None) -> np.ndarray:
 def sum_abs(x, axis) -> np.ndarray:
     """sum(|x|): the scale fp32 summation error is measured against."""
     return np.sum(np.abs(np.asarray(x, np.float64)), axis=axis)
+
+
+# --------------------------------------------------------------- backward ---
+# The gradients of the fused formulas, fp64 math, one rounding.  They restate
+# what torch autograd computes through the HF modules (the reference trains
+# through those: pow/mean/rsqrt/mul backward for RMSNorm, silu_backward
+# csrc/aten/backends/cuda/silu_backward.cu:15-35, softmax backward).
+
+
+def rms_norm_bwd_golden(x, w, dy, eps: float, dtype: str):
+    """(dx, dw) of out = w * x * r, r = 1/sqrt(mean(x^2) + eps) over the last
+    dim: dx = r (w dy - n mean(w dy n)), n = x r; dw = sum over rows dy n."""
+    x64 = np.asarray(x, np.float64)
+    w64 = np.asarray(w, np.float64)
+    g64 = np.asarray(dy, np.float64)
+    r = 1.0 / np.sqrt(np.mean(x64 * x64, axis=-1, keepdims=True) + eps)
+    n = x64 * r
+    m = np.mean(w64 * g64 * n, axis=-1, keepdims=True)
+    dx = r * (w64 * g64 - n * m)
+    dw = np.sum((g64 * n).reshape(-1, x64.shape[-1]), axis=0)
+    return round_to(dx, dtype), round_to(dw, dtype)
+
+
+def rms_norm_bwd_bound(x, w, dy, eps: float) -> np.ndarray:
+    """Magnitude of the terms of dx, r (|w dy| + |n| mean(|w dy n|)): an fp32
+    evaluation is within a few 2^-24 of this (the mean is a sum that can
+    cancel, so its error scales with the sum of magnitudes), so tests scale
+    their absolute tolerance by it."""
+    x64 = np.asarray(x, np.float64)
+    w64 = np.asarray(w, np.float64)
+    g64 = np.asarray(dy, np.float64)
+    r = 1.0 / np.sqrt(np.mean(x64 * x64, axis=-1, keepdims=True) + eps)
+    n = x64 * r
+    m_abs = np.mean(np.abs(w64 * g64 * n), axis=-1, keepdims=True)
+    return r * (np.abs(w64 * g64) + np.abs(n) * m_abs)
+
+
+def _sigmoid64(g):
+    return 1.0 / (1.0 + np.exp(-g))
+
+
+def swiglu_bwd_golden(dout, g, u, dtype: str):
+    """(dgate, dup) of silu(g) * u: dup = dout silu(g),
+    dgate = dout u s (1 + g (1 - s)), s = sigmoid(g)."""
+    d64 = np.asarray(dout, np.float64)
+    g64 = np.asarray(g, np.float64)
+    u64 = np.asarray(u, np.float64)
+    with np.errstate(over="ignore", invalid="ignore"):
+        s = _sigmoid64(g64)
+        dg = d64 * u64 * s * (1.0 + g64 * (1.0 - s))
+        du = d64 * g64 * s
+    return round_to(dg, dtype), round_to(du, dtype)
+
+
+def silu_bwd_golden(dout, x, dtype: str):
+    """silu_backward: dout * s * (1 + x (1 - s)) (silu_backward.cu:27-31)."""
+    d64 = np.asarray(dout, np.float64)
+    x64 = np.asarray(x, np.float64)
+    with np.errstate(over="ignore", invalid="ignore"):
+        s = _sigmoid64(x64)
+        return round_to(d64 * s * (1.0 + x64 * (1.0 - s)), dtype)
+
+
+def softmax_bwd_golden(dy, y, dtype: str):
+    """dx = y (dy - sum(dy y)) over the last dim."""
+    g64 = np.asarray(dy, np.float64)
+    y64 = np.asarray(y, np.float64)
+    return round_to(y64 * (g64 - np.sum(g64 * y64, axis=-1, keepdims=True)), dtype)
+
+
+def softmax_bwd_bound(dy, y) -> np.ndarray:
+    """Magnitude of the terms of the softmax gradient, |y| (|dy| + sum |dy y|)
+    (the sum can cancel, so its error scales with the sum of magnitudes)."""
+    g64 = np.asarray(dy, np.float64)
+    y64 = np.asarray(y, np.float64)
+    return np.abs(y64) * (np.abs(g64) + np.sum(np.abs(g64 * y64), axis=-1, keepdims=True))
+
+
+def rope_bwd_golden(dq_out, cos, sin, dtype: str):
+    """Gradient of x cos + rotate_half(x) sin w.r.t. x: dq_out cos +
+    rotate_half^T(dq_out sin), rotate_half^T(v) = cat(v2, -v1)."""
+    d64 = np.asarray(dq_out, np.float64)
+    c64 = np.asarray(cos, np.float64)
+    s64 = np.asarray(sin, np.float64)
+    t = d64 * s64
+    h = t.shape[-1] // 2
+    rt = np.concatenate([t[..., h:], -t[..., :h]], axis=-1)
+    return round_to(d64 * c64 + rt, dtype)

@@ -223,6 +223,76 @@ at::Tensor CausalSoftmax(const at::Tensor& x_in, int64_t offset, std::optional<a
   return out;
 }
 
+// -------------------------------------------------------------- backward --
+// The backward ops the autograd formulas of the fused ops call
+// (torch_fl/autograd.py).  fp32 math, one rounding to the output dtype.
+std::tuple<at::Tensor, at::Tensor> RmsNormBackward(const at::Tensor& dy_in,
+                                                   const at::Tensor& x_in,
+                                                   const at::Tensor& weight, double eps) {
+  const char* op = "flagos::rms_norm_backward";
+  const int code = FloatCode(x_in, op);
+  SameDevice(x_in, dy_in, op);
+  SameDevice(x_in, weight, op);
+  TORCH_CHECK(dy_in.sizes() == x_in.sizes() && dy_in.scalar_type() == x_in.scalar_type(), op,
+              ": dy and x must match");
+  TORCH_CHECK(weight.scalar_type() == x_in.scalar_type() && weight.dim() == 1 &&
+                  weight.numel() == x_in.size(-1),
+              op, ": weight must be a [hidden] tensor of x's dtype");
+  at::Tensor x, dy;
+  const RowsView r = Rows(x_in, x), rd = Rows(dy_in, dy);
+  at::Tensor w = weight.contiguous();
+  at::Tensor dx = at::empty(x.sizes(), x.options());
+  at::Tensor dw = at::empty({r.cols}, w.options());
+  GpuGuard g(x);
+  const size_t nws = fl_b200_rms_norm_bwd_workspace_size(r.rows, r.cols);
+  at::Tensor ws = at::empty({(int64_t)std::max<size_t>(nws, 16)}, x.options().dtype(at::kByte));
+  CheckB200(fl_b200_rms_norm_bwd(dy.data_ptr(), rd.ld, x.data_ptr(), r.ld, w.data_ptr(),
+                                 dx.data_ptr(), r.cols, dw.data_ptr(), r.rows, r.cols, (float)eps,
+                                 code, ws.data_ptr(), nws, StreamOf(x)),
+            op);
+  return {dx, dw};
+}
+
+std::tuple<at::Tensor, at::Tensor> SwigluBackward(const at::Tensor& dout, const at::Tensor& gate,
+                                                  const at::Tensor& up) {
+  const char* op = "flagos::swiglu_backward";
+  const int code = FloatCode(gate, op);
+  SameDevice(gate, up, op);
+  SameDevice(gate, dout, op);
+  TORCH_CHECK(gate.sizes() == up.sizes() && gate.sizes() == dout.sizes() &&
+                  up.scalar_type() == gate.scalar_type() &&
+                  dout.scalar_type() == gate.scalar_type(),
+              op, ": dout, gate and up must match");
+  at::Tensor d = dout.contiguous(), g = gate.contiguous(), u = up.contiguous();
+  at::Tensor dg = at::empty(g.sizes(), g.options()), du = at::empty(u.sizes(), u.options());
+  GpuGuard guard(g);
+  CheckB200(fl_b200_swiglu_bwd(d.data_ptr(), g.data_ptr(), u.data_ptr(), dg.data_ptr(),
+                               du.data_ptr(), g.numel(), code, StreamOf(g)),
+            op);
+  return {dg, du};
+}
+
+at::Tensor SoftmaxBackward(const at::Tensor& dy_in, const at::Tensor& y_in,
+                           std::optional<at::ScalarType> dtype) {
+  const char* op = "flagos::softmax_backward";
+  const int ci = FloatCode(y_in, op);
+  SameDevice(y_in, dy_in, op);
+  TORCH_CHECK(dy_in.sizes() == y_in.sizes() && dy_in.scalar_type() == y_in.scalar_type(), op,
+              ": dy and y must match");
+  const at::ScalarType ot = dtype.value_or(y_in.scalar_type());
+  const int co = B200Dtype(ot);
+  TORCH_CHECK(co == ci || (ci == FL_B200_F32 && (co == FL_B200_BF16 || co == FL_B200_F16)), op,
+              ": output dtype must be y's, or 16-bit with float32 y");
+  at::Tensor y, dy;
+  const RowsView r = Rows(y_in, y), rd = Rows(dy_in, dy);
+  at::Tensor dx = at::empty(y.sizes(), y.options().dtype(ot));
+  GpuGuard g(y);
+  CheckB200(fl_b200_softmax_bwd(dy.data_ptr(), rd.ld, y.data_ptr(), r.ld, dx.data_ptr(), r.cols,
+                                r.rows, r.cols, ci, co, StreamOf(y)),
+            op);
+  return dx;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(flagos, m) {
@@ -237,6 +307,9 @@ TORCH_LIBRARY(flagos, m) {
   m.def("swiglu_residual(Tensor gate, Tensor up, Tensor x, Tensor y, str rounding='fused') "
         "-> (Tensor, Tensor)");
   m.def("causal_softmax(Tensor x, int offset=0, ScalarType? dtype=None) -> Tensor");
+  m.def("rms_norm_backward(Tensor dy, Tensor x, Tensor weight, float eps) -> (Tensor, Tensor)");
+  m.def("swiglu_backward(Tensor dout, Tensor gate, Tensor up) -> (Tensor, Tensor)");
+  m.def("softmax_backward(Tensor dy, Tensor y, ScalarType? dtype=None) -> Tensor");
 }
 
 #define FLB_FUSED_IMPLS(m)                          \
@@ -246,7 +319,10 @@ TORCH_LIBRARY(flagos, m) {
   m.impl("rms_norm_rope", RmsNormRope);             \
   m.impl("swiglu", Swiglu);                         \
   m.impl("swiglu_residual", SwigluResidual);        \
-  m.impl("causal_softmax", CausalSoftmax);
+  m.impl("causal_softmax", CausalSoftmax);          \
+  m.impl("rms_norm_backward", RmsNormBackward);     \
+  m.impl("swiglu_backward", SwigluBackward);        \
+  m.impl("softmax_backward", SoftmaxBackward);
 
 TORCH_LIBRARY_IMPL(flagos, PrivateUse1, m) { FLB_FUSED_IMPLS(m) }
 TORCH_LIBRARY_IMPL(flagos, CUDA, m) { FLB_FUSED_IMPLS(m) }

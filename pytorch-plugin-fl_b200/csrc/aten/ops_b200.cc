@@ -122,6 +122,53 @@ at::Tensor SoftmaxB200(const at::Tensor& self, int64_t dim, bool half_to_float) 
   return out;
 }
 
+// ------------------------------------------------------------- backward --
+// _softmax_backward_data: dx = y * (dy - sum(dy * y)) along dim, in
+// input_dtype.  Last dim on the b200 kernel; another dim moves to the last
+// place (a copy each way) so the same kernel runs.
+at::Tensor SoftmaxBackwardB200(const at::Tensor& grad, const at::Tensor& output, int64_t dim,
+                               at::ScalarType input_dtype) {
+  const char* name = "_softmax_backward_data";
+  const at::ScalarType t = output.scalar_type();
+  TORCH_CHECK(IsFloat(t) && grad.scalar_type() == t, name,
+              " (b200 route): grad and output must share a floating dtype");
+  TORCH_CHECK(grad.sizes() == output.sizes(), name, ": grad and output shapes differ");
+  TORCH_CHECK(IsFloat(input_dtype) && (input_dtype == t || t == at::kFloat), name,
+              ": input_dtype must be the output's dtype, or 16-bit with float32 grads");
+  if (output.dim() == 0) return at::zeros({}, output.options().dtype(input_dtype));
+  dim = at::maybe_wrap_dim(dim, output.dim());
+  const bool last = dim == output.dim() - 1;
+  at::Tensor g = (last ? grad : grad.movedim(dim, -1)).contiguous();
+  at::Tensor y = (last ? output : output.movedim(dim, -1)).contiguous();
+  at::Tensor dx = at::empty(y.sizes(), y.options().dtype(input_dtype));
+  if (y.numel() > 0) {
+    GpuGuard gd(y);
+    const int64_t n = y.size(-1), rows = y.numel() / n;
+    CheckB200(fl_b200_softmax_bwd(g.data_ptr(), n, y.data_ptr(), n, dx.data_ptr(), n, rows, n,
+                                  B200Dtype(t), B200Dtype(input_dtype), StreamOf(y)),
+              name);
+  }
+  return last ? dx : dx.movedim(-1, dim).contiguous();
+}
+
+// silu_backward: dx = grad * s * (1 + x (1 - s)), s = sigmoid(x).
+at::Tensor SiluBackwardB200(const at::Tensor& grad, const at::Tensor& self) {
+  const char* name = "silu_backward";
+  const at::ScalarType t = self.scalar_type();
+  TORCH_CHECK(IsFloat(t) && grad.scalar_type() == t, name,
+              " (b200 route): grad and input must share a floating dtype");
+  TORCH_CHECK(grad.sizes() == self.sizes(), name, ": grad and input shapes differ");
+  at::Tensor g = grad.contiguous(), x = self.contiguous();
+  at::Tensor dx = at::empty(x.sizes(), x.options());
+  if (x.numel() > 0) {
+    GpuGuard gd(x);
+    CheckB200(fl_b200_silu_bwd(g.data_ptr(), x.data_ptr(), dx.data_ptr(), x.numel(),
+                               B200Dtype(t), StreamOf(x)),
+              name);
+  }
+  return dx;
+}
+
 // ------------------------------------------------------------- reductions --
 enum class Red { kSum, kMean, kAmax, kArgmax };
 
@@ -309,5 +356,8 @@ FLB_REGISTER_KERNEL(ReduceDimFn, sum_dim_dispatcher, Backend::kB200, SumDimB200)
 FLB_REGISTER_KERNEL(ReduceDimFn, mean_dim_dispatcher, Backend::kB200, MeanDimB200)
 FLB_REGISTER_KERNEL(AmaxFn, amax_dispatcher, Backend::kB200, AmaxB200)
 FLB_REGISTER_KERNEL(ArgmaxFn, argmax_dispatcher, Backend::kB200, ArgmaxB200)
+FLB_REGISTER_KERNEL(SoftmaxBackwardFn, softmax_backward_dispatcher, Backend::kB200,
+                    SoftmaxBackwardB200)
+FLB_REGISTER_KERNEL(SiluBackwardFn, silu_backward_dispatcher, Backend::kB200, SiluBackwardB200)
 
 }  // namespace flb200::aten

@@ -24,6 +24,8 @@ FLB_DEFINE_DISPATCHER(UnaryFn, cos_dispatcher, "cos")
 FLB_DEFINE_DISPATCHER(UnaryFn, sin_dispatcher, "sin")
 FLB_DEFINE_DISPATCHER(PowScalarFn, pow_tensor_scalar_dispatcher, "pow.Tensor_Scalar")
 FLB_DEFINE_DISPATCHER(CatFn, cat_dispatcher, "cat")
+FLB_DEFINE_DISPATCHER(SoftmaxBackwardFn, softmax_backward_dispatcher, "_softmax_backward_data")
+FLB_DEFINE_DISPATCHER(SiluBackwardFn, silu_backward_dispatcher, "silu_backward")
 
 namespace {
 
@@ -70,6 +72,14 @@ at::Tensor CatCuda(const at::ITensorListRef& ts, int64_t dim) {
   return ToFlagos(at::cat(v, dim));
 }
 
+at::Tensor SoftmaxBackwardCuda(const at::Tensor& g, const at::Tensor& y, int64_t dim,
+                               at::ScalarType input_dtype) {
+  return ToFlagos(at::_softmax_backward_data(CudaAlias(g), CudaAlias(y), dim, input_dtype));
+}
+at::Tensor SiluBackwardCuda(const at::Tensor& g, const at::Tensor& x) {
+  return ToFlagos(at::silu_backward(CudaAlias(g), CudaAlias(x)));
+}
+
 }  // namespace
 
 FLB_REGISTER_KERNEL(AddTensorFn, add_tensor_dispatcher, Backend::kCuda, AddTensorCuda)
@@ -88,5 +98,8 @@ FLB_REGISTER_KERNEL(UnaryFn, cos_dispatcher, Backend::kCuda, CosCuda)
 FLB_REGISTER_KERNEL(UnaryFn, sin_dispatcher, Backend::kCuda, SinCuda)
 FLB_REGISTER_KERNEL(PowScalarFn, pow_tensor_scalar_dispatcher, Backend::kCuda, PowScalarCuda)
 FLB_REGISTER_KERNEL(CatFn, cat_dispatcher, Backend::kCuda, CatCuda)
+FLB_REGISTER_KERNEL(SoftmaxBackwardFn, softmax_backward_dispatcher, Backend::kCuda,
+                    SoftmaxBackwardCuda)
+FLB_REGISTER_KERNEL(SiluBackwardFn, silu_backward_dispatcher, Backend::kCuda, SiluBackwardCuda)
 
 }  // namespace flb200::aten

@@ -198,6 +198,13 @@ at::Tensor PowTensorScalar(const at::Tensor& x, const at::Scalar& e) {
   return pow_tensor_scalar_dispatcher(x, e);
 }
 at::Tensor Cat(const at::ITensorListRef& ts, int64_t dim) { return cat_dispatcher(ts, dim); }
+at::Tensor SoftmaxBackwardData(const at::Tensor& g, const at::Tensor& y, int64_t dim,
+                               at::ScalarType input_dtype) {
+  return softmax_backward_dispatcher(g, y, dim, input_dtype);
+}
+at::Tensor SiluBackward(const at::Tensor& g, const at::Tensor& x) {
+  return silu_backward_dispatcher(g, x);
+}
 
 // ------------------------------------------------------------- fallback ---
 // A CUDA alias whose storage may be resized by an out= kernel: the resized
@@ -305,6 +312,8 @@ TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
   m.impl("sin", Sin);
   m.impl("pow.Tensor_Scalar", PowTensorScalar);
   m.impl("cat", Cat);
+  m.impl("_softmax_backward_data", SoftmaxBackwardData);
+  m.impl("silu_backward", SiluBackward);
 }
 
 TORCH_LIBRARY_IMPL(_, PrivateUse1, m) {

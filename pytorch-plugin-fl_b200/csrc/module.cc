@@ -39,6 +39,8 @@ std::map<std::string, std::string> Routes() {
   add(A::sin_dispatcher);
   add(A::pow_tensor_scalar_dispatcher);
   add(A::cat_dispatcher);
+  add(A::softmax_backward_dispatcher);
+  add(A::silu_backward_dispatcher);
   return r;
 }
 

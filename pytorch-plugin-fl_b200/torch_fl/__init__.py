@@ -24,6 +24,9 @@ torch._register_device_module("flagos", flagos)
 torch.utils.generate_methods_for_privateuse1_backend(for_storage=True)
 
 from . import kernels, ops  # noqa: E402
+from . import autograd as _autograd  # noqa: E402
+
+_autograd.register()  # backward formulas of the flagos:: fused ops
 from .integration import (  # noqa: E402
     disable_hf_fused_ops,
     enable_hf_fused_ops,

@@ -66,6 +66,12 @@ PROTOTYPES: dict[str, tuple] = {
     "fl_b200_argmax_lastdim": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _p, _sz, _p]),
     "fl_b200_sum_i32_i64": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _p, _sz, _p]),
     "fl_b200_reduce_sum_all_noalloc": (_i32, [_p, _i64, _p, _i32, _i32, _p]),
+    "fl_b200_rms_norm_bwd_workspace_size": (_sz, [_i64, _i64]),
+    "fl_b200_rms_norm_bwd": (
+        _i32, [_p, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _i64, _f32, _i32, _p, _sz, _p]),
+    "fl_b200_swiglu_bwd": (_i32, [_p, _p, _p, _p, _p, _i64, _i32, _p]),
+    "fl_b200_silu_bwd": (_i32, [_p, _p, _p, _i64, _i32, _p]),
+    "fl_b200_softmax_bwd": (_i32, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i32, _i32, _p]),
 }
 
 

@@ -8,8 +8,9 @@ aten op for the flagos device.
 it replaces, in the installed transformers, the forward of the RMSNorm
 modules, the module-level `apply_rotary_pos_emb`, and the SwiGLU MLP forward
 of the Qwen3 / Qwen2 / Llama / Mistral model files with the flagos:: fused
-kernels.  The hooks act on device tensors (flagos or cuda) that need no
-gradient; anything else (CPU tensors, training with autograd) runs the
+kernels.  The hooks act on device tensors (flagos or cuda), in inference and
+in training (the fused ops carry autograd formulas, torch_fl/autograd.py);
+CPU tensors, and RoPE tables that themselves need a gradient, run the
 original HF code unchanged.  `disable_hf_fused_ops()` restores the originals.
 """
 
@@ -60,7 +61,7 @@ def _fusable(*tensors) -> bool:
             return False
         if t.dtype not in (torch.float32, torch.bfloat16, torch.float16):
             return False
-    return not (torch.is_grad_enabled() and any(t.requires_grad for t in tensors))
+    return True
 
 
 def _rms_forward(orig):
@@ -77,8 +78,9 @@ def _rms_forward(orig):
 def _rope_fn(orig):
     def apply_rotary_pos_emb(q, k, cos, sin, *args, **kwargs):
         unsqueeze_dim = kwargs.get("unsqueeze_dim", args[-1] if args and isinstance(args[-1], int) else 1)
+        tables_need_grad = torch.is_grad_enabled() and (cos.requires_grad or sin.requires_grad)
         if (_fusable(q, k, cos, sin) and q.dim() == 4 and q.dtype == cos.dtype == k.dtype
-                and unsqueeze_dim in (1, 2)):
+                and unsqueeze_dim in (1, 2) and not tables_need_grad):
             return ops.rope_qk(q, k, cos, sin, unsqueeze_dim, _rounding)
         return orig(q, k, cos, sin, *args, **kwargs)
 

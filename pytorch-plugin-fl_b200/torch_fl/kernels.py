@@ -435,3 +435,72 @@ def sum_i32_i64(x: torch.Tensor, full: bool) -> torch.Tensor:
         _abi.call("fl_b200_sum_i32_i64", x.data_ptr(), ld, rows, cols, out.data_ptr(),
                   int(full), wsp, wsn, _stream(x))
     return out
+
+
+# -------------------------------------------------------------------- backward
+def rms_norm_backward(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, eps: float,
+                      need_dw: bool = True) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """(dx, dw) of out = weight * x * rsqrt(mean(x^2) + eps) over the last dim;
+    dw is None when not need_dw.  fp32 math, deterministic dw."""
+    if dy.shape != x.shape or dy.dtype != x.dtype:
+        raise ValueError("dy and x must match")
+    x, rows, cols, ldx = _rows_or_contig(x)
+    dy, _, _, lddy = _rows_or_contig(dy)
+    if weight.dtype != x.dtype or weight.numel() != cols or not weight.is_contiguous():
+        raise ValueError("weight must be a contiguous [cols] tensor of x's dtype")
+    dx = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    _, _, lddx = _rows_view(dx)
+    dw = torch.empty(cols, dtype=x.dtype, device=x.device) if need_dw else None
+    with _on_device(x):
+        ws, nws = None, 0
+        if need_dw:
+            nws = _abi.lib().fl_b200_rms_norm_bwd_workspace_size(rows, cols)
+            ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=x.device) if nws else None
+        _abi.call("fl_b200_rms_norm_bwd", dy.data_ptr(), lddy, x.data_ptr(), ldx,
+                  weight.data_ptr(), dx.data_ptr(), lddx, dw.data_ptr() if need_dw else None,
+                  rows, cols, float(eps), dtype_code(x), ws.data_ptr() if ws is not None else None,
+                  nws, _stream(x))
+    return dx, dw
+
+
+def swiglu_backward(dout: torch.Tensor, gate: torch.Tensor,
+                    up: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(dgate, dup) of out = silu(gate) * up."""
+    if not (dout.shape == gate.shape == up.shape) or not (dout.dtype == gate.dtype == up.dtype):
+        raise ValueError("dout, gate and up must match")
+    dout, gate, up = dout.contiguous(), gate.contiguous(), up.contiguous()
+    dg, du = torch.empty_like(gate), torch.empty_like(up)
+    with _on_device(gate):
+        _abi.call("fl_b200_swiglu_bwd", dout.data_ptr(), gate.data_ptr(), up.data_ptr(),
+                  dg.data_ptr(), du.data_ptr(), gate.numel(), dtype_code(gate), _stream(gate))
+    return dg, du
+
+
+def silu_backward(dout: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """d silu(x) = dout * s * (1 + x (1 - s)), s = sigmoid(x)."""
+    if dout.shape != x.shape or dout.dtype != x.dtype:
+        raise ValueError("dout and x must match")
+    dout, x = dout.contiguous(), x.contiguous()
+    dx = torch.empty_like(x)
+    with _on_device(x):
+        _abi.call("fl_b200_silu_bwd", dout.data_ptr(), x.data_ptr(), dx.data_ptr(), x.numel(),
+                  dtype_code(x), _stream(x))
+    return dx
+
+
+def softmax_backward(dy: torch.Tensor, y: torch.Tensor,
+                     out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """dx = y * (dy - sum(dy * y)) over the last dim; out_dtype defaults to
+    y's dtype (a 16-bit dtype with fp32 dy/y: half_to_float's backward)."""
+    if dy.shape != y.shape or dy.dtype != y.dtype:
+        raise ValueError("dy and y must match")
+    out_dtype = out_dtype or y.dtype
+    if y.dim() == 0:
+        return torch.zeros((), dtype=out_dtype, device=y.device)
+    y, rows, cols, ldy = _rows_or_contig(y)
+    dy, _, _, lddy = _rows_or_contig(dy)
+    dx = torch.empty(y.shape, dtype=out_dtype, device=y.device)
+    with _on_device(y):
+        _abi.call("fl_b200_softmax_bwd", dy.data_ptr(), lddy, y.data_ptr(), ldy, dx.data_ptr(),
+                  cols, rows, cols, dtype_code(y), _DT[out_dtype], _stream(y))
+    return dx

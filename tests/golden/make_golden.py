@@ -209,6 +209,62 @@ def main() -> None:
     _store(d, "mul_bf16/w_h", wv * hv)
     _store(d, "mul_bf16/h_c", hv * cv)
 
+    # --- backward: torch CPU autograd of the same modules, fp32 -------------
+    # RMSNorm (Qwen3RMSNorm: dx and the weight gradient)
+    g = _gen(10)
+    x = torch.randn(16, 512, generator=g)
+    w = 1 + 0.1 * torch.randn(512, generator=g)
+    dy = torch.randn(16, 512, generator=g)
+    mod = mq.Qwen3RMSNorm(512, eps=1e-6)
+    with torch.no_grad():
+        mod.weight.copy_(w)
+    xg = x.clone().requires_grad_(True)
+    mod(xg).backward(dy)
+    for k_, t in (("x", x), ("w", w), ("dy", dy), ("dx", xg.grad), ("dw", mod.weight.grad)):
+        _store(d, f"rmsnorm_bwd_f32/{k_}", t)
+
+    # SwiGLU: act_fn(gate) * up
+    g = _gen(11)
+    gate = 3.0 * torch.randn(16, 1024, generator=g)
+    up = torch.randn(16, 1024, generator=g)
+    dact = torch.randn(16, 1024, generator=g)
+    gg, ug = gate.clone().requires_grad_(True), up.clone().requires_grad_(True)
+    (ACT2FN["silu"](gg) * ug).backward(dact)
+    for k_, t in (("gate", gate), ("up", up), ("dout", dact), ("dgate", gg.grad),
+                  ("dup", ug.grad)):
+        _store(d, f"swiglu_bwd_f32/{k_}", t)
+
+    # softmax over the last dim, fp32; and the half_to_float variant (bf16
+    # logits, fp32 probabilities as HF eager attention computes them)
+    g = _gen(12)
+    xs = 3.0 * torch.randn(8, 256, generator=g)
+    dys = torch.randn(8, 256, generator=g)
+    xsg = xs.clone().requires_grad_(True)
+    torch.softmax(xsg, dim=-1).backward(dys)
+    for k_, t in (("x", xs), ("dy", dys), ("dx", xsg.grad)):
+        _store(d, f"softmax_bwd_f32/{k_}", t)
+    xh = (3.0 * torch.randn(8, 256, generator=g)).to(torch.bfloat16)
+    dyh = torch.randn(8, 256, generator=g)
+    xhg = xh.clone().requires_grad_(True)
+    yh = torch.softmax(xhg, dim=-1, dtype=torch.float32)
+    yh.backward(dyh)
+    for k_, t in (("x", xh), ("y", yh.detach()), ("dy", dyh), ("dx", xhg.grad)):
+        _store(d, f"softmax_bwd_half_to_float/{k_}", t)
+
+    # RoPE: apply_rotary_pos_emb, fp32 q/k, the fp32 HF tables
+    g = _gen(13)
+    cosf, sinf = hf_chain.rope_tables(pos, 128, 10000.0, torch.float32)
+    qf = torch.randn(1, 4, S, 128, generator=g)
+    kf = torch.randn(1, 2, S, 128, generator=g)
+    dq_o = torch.randn(1, 4, S, 128, generator=g)
+    dk_o = torch.randn(1, 2, S, 128, generator=g)
+    qg, kg = qf.clone().requires_grad_(True), kf.clone().requires_grad_(True)
+    qo_, ko_ = mq.apply_rotary_pos_emb(qg, kg, cosf, sinf)
+    torch.autograd.backward([qo_, ko_], [dq_o, dk_o])
+    for k_, t in (("q", qf), ("k", kf), ("cos", cosf), ("sin", sinf), ("dq_out", dq_o),
+                  ("dk_out", dk_o), ("dq", qg.grad), ("dk", kg.grad)):
+        _store(d, f"rope_bwd_f32/{k_}", t)
+
     np.savez_compressed(OUT, **d)
     print(f"wrote {OUT}: {len(d)} arrays, {os.path.getsize(OUT)} bytes")
 

@@ -94,6 +94,41 @@ def assert_rel(got, ref, rtol: float = REL_TOL, atol: float = 0.0, what: str = "
                              f"got {got[i]!r} want {ref[i]!r}")
 
 
+# Gradients whose terms can cancel (RMSNorm dx = r (w dy - n m), softmax
+# dx = y (dy - sum dy y)) are checked against an elementwise bound scaled by
+# the magnitude of the terms: an fp32 evaluation is within a few 2^-24 of
+# that magnitude, however small the result.  BWD_TERM_TOL is that factor;
+# the storage rounding (1 ulp of the output dtype) comes on top.
+BWD_TERM_TOL = 64 * 2.0 ** -24
+
+
+def ulp_of(ref, dtype: str) -> np.ndarray:
+    """Spacing of the storage dtype at |ref| (its unit in the last place)."""
+    r = np.abs(np.asarray(ref, np.float64)).astype(np.float32)
+    if dtype == "f16":
+        return np.spacing(r.astype(np.float16)).astype(np.float64)
+    sp = np.spacing(r).astype(np.float64)
+    return sp * 2.0 ** 16 if dtype == "bf16" else sp
+
+
+def assert_within(got, ref, tol, what: str = "", dtype: str | None = None) -> None:
+    """|got - ref| <= tol elementwise (tol broadcasts); with a 16-bit `dtype`
+    the final rounding adds 1 ulp of ref to the tolerance."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert got.shape == ref.shape, (what, got.shape, ref.shape)
+    err = np.abs(got - ref)
+    lim = np.broadcast_to(tol, err.shape).astype(np.float64)
+    if dtype in ("bf16", "f16"):
+        lim = lim + ulp_of(ref, dtype)
+    ok = (err <= lim) | (np.isnan(got) & np.isnan(ref))
+    if not np.all(ok):
+        i = tuple(np.argwhere(~ok)[0])
+        t = lim[i]
+        raise AssertionError(f"{what}: err {err[i]:.3g} > tol {t:.3g} at {i}: "
+                             f"got {got[i]!r} want {ref[i]!r}")
+
+
 def assert_sum(got, x, axis, what: str = "", tol: float = SUM_TOL) -> None:
     x64 = np.asarray(x, np.float64)
     exact = np.sum(x64, axis=axis)

@@ -80,7 +80,7 @@ def test_qwen3_bf16_hooks_match_unhooked():
     assert (fused - plain).abs().max() <= 0.05 * scale
 
 
-def test_hooks_leave_cpu_and_autograd_paths_alone():
+def test_hooks_leave_cpu_paths_alone():
     model = tiny_qwen3(torch.float32)
     torch_fl.enable_hf_fused_ops()
     ids = torch.randint(0, 512, (1, 16))
@@ -88,3 +88,32 @@ def test_hooks_leave_cpu_and_autograd_paths_alone():
     out.sum().backward()             # and autograd works
     assert model.model.norm.weight.grad is not None
     integration.disable_hf_fused_ops()
+
+
+@pytest.mark.parametrize("hooks", [True, False])
+def test_qwen3_training_step_on_flagos_matches_cpu(hooks):
+    """One forward + backward of a causal-LM loss on flagos:0: with the hooks
+    the fused ops and their backward kernels run (RMSNorm, RoPE, SwiGLU);
+    without them the aten ops do (silu_backward and _softmax_backward_data on
+    the b200 route).  Loss and every parameter gradient match the same model
+    on the CPU."""
+    import copy
+
+    cpu = tiny_qwen3(torch.float32).train()
+    dev = copy.deepcopy(cpu).to("flagos")
+    ids = torch.randint(0, 512, (2, 32), generator=torch.Generator().manual_seed(3))
+    if hooks:
+        torch_fl.enable_hf_fused_ops()
+    loss_d = dev(ids.to("flagos"), labels=ids.to("flagos")).loss
+    loss_d.backward()
+    loss_c = cpu(ids, labels=ids).loss       # CPU tensors: the original HF code
+    loss_c.backward()
+    torch.testing.assert_close(loss_d.cpu(), loss_c, rtol=1e-5, atol=1e-5)
+    n = 0
+    for (name, pd), (_, pc) in zip(dev.named_parameters(), cpu.named_parameters()):
+        assert pd.grad is not None, name
+        scale = pc.grad.abs().max().item() + 1e-12
+        torch.testing.assert_close(pd.grad.cpu(), pc.grad, rtol=1e-3, atol=1e-4 * scale,
+                                   msg=lambda m, name=name: f"{name}: {m}")
+        n += 1
+    assert n > 10

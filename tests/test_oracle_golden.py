@@ -143,3 +143,55 @@ def test_ulp_distance(dtype):
     step = 2.0 ** -7 if dtype == "bf16" else 2.0 ** -10
     b = ops.round_to(np.array([1.0 + step, -1.0 - step, -0.0, 3.0], np.float32), dtype)
     assert list(ops.ulp_diff(a, b, dtype)) == [1, 1, 0, 0]
+
+
+# --------------------------------------------------------------- backward ---
+# torch CPU autograd of the transformers modules (fp32) against the oracle's
+# fp64 gradients: agreement to fp32 accuracy, scaled by the magnitude of the
+# terms where they cancel.
+
+
+def test_rmsnorm_backward_oracle_matches_autograd(golden):
+    x, w, dy = (golden.get(f"rmsnorm_bwd_f32/{k}") for k in ("x", "w", "dy"))
+    dx, dw = ops.rms_norm_bwd_golden(x, w, dy, 1e-6, "f32")
+    bound = ops.rms_norm_bwd_bound(x, w, dy, 1e-6)
+    parity.assert_within(dx, golden.get("rmsnorm_bwd_f32/dx"), 4 * parity.BWD_TERM_TOL * bound,
+                         "dx")
+    r = 1.0 / np.sqrt(np.mean(x.astype(np.float64) ** 2, -1, keepdims=True) + 1e-6)
+    terms = np.sum(np.abs(dy * x * r), axis=0)
+    parity.assert_within(dw, golden.get("rmsnorm_bwd_f32/dw"), 1e-5 * terms, "dw")
+
+
+def test_swiglu_backward_oracle_matches_autograd(golden):
+    g, u, d = (golden.get(f"swiglu_bwd_f32/{k}") for k in ("gate", "up", "dout"))
+    dg, du = ops.swiglu_bwd_golden(d, g, u, "f32")
+    scale = np.abs(d) * (np.abs(u) * (1 + np.abs(g)) + np.abs(g))
+    parity.assert_within(dg, golden.get("swiglu_bwd_f32/dgate"), 1e-6 * scale, "dgate")
+    parity.assert_within(du, golden.get("swiglu_bwd_f32/dup"), 1e-6 * scale, "dup")
+    # the silu part alone is silu_backward (dout * u as its incoming grad)
+    parity.assert_within(ops.silu_bwd_golden(d * u, g, "f32"),
+                         golden.get("swiglu_bwd_f32/dgate"), 1e-6 * scale, "silu_backward")
+
+
+def test_softmax_backward_oracle_matches_autograd(golden):
+    x, dy = golden.get("softmax_bwd_f32/x"), golden.get("softmax_bwd_f32/dy")
+    y = ops.softmax_golden(x, "f32")
+    parity.assert_within(ops.softmax_bwd_golden(dy, y, "f32"), golden.get("softmax_bwd_f32/dx"),
+                         4 * parity.BWD_TERM_TOL * ops.softmax_bwd_bound(dy, y), "dx")
+    # half_to_float: fp32 probabilities and grads back to bf16 logits
+    y, dy = golden.get("softmax_bwd_half_to_float/y"), golden.get("softmax_bwd_half_to_float/dy")
+    parity.assert_within(ops.softmax_bwd_golden(dy, y, "bf16"),
+                         golden.get("softmax_bwd_half_to_float/dx"),
+                         4 * parity.BWD_TERM_TOL * ops.softmax_bwd_bound(dy, y), "dx bf16",
+                         dtype="bf16")
+
+
+def test_rope_backward_oracle_matches_autograd(golden):
+    cos, sin = golden.get("rope_bwd_f32/cos")[:, None], golden.get("rope_bwd_f32/sin")[:, None]
+    for name in ("q", "k"):
+        d = golden.get(f"rope_bwd_f32/d{name}_out")
+        got = ops.rope_bwd_golden(d, cos, sin, "f32")
+        parity.assert_rel(got, golden.get(f"rope_bwd_f32/d{name}"), rtol=1e-6, atol=1e-6, what=name)
+        # the adjoint is the forward rotation with -sin (cos/sin halves repeat)
+        parity.assert_rel(ops.rope_golden(d, cos, -sin, "f32"), got, rtol=1e-7, atol=1e-7,
+                          what=f"{name} via -sin")

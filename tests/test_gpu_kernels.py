@@ -400,6 +400,28 @@ def test_softmax_row_rungs(dtype, cols):
         check_float(got, ref, dt, f"causal {cols} off={off}")
 
 
+@pytest.mark.parametrize("causal", [False, True])
+def test_softmax_f32_out_both_store_widths(causal):
+    """fp32 output of 16-bit rows goes out as 32-byte stores when the output
+    is 32-byte aligned and as 16-byte stores otherwise; both match the oracle."""
+    from torch_fl import _abi
+
+    rows, cols = 96, 2048
+    x = rnd((rows, cols), torch.bfloat16, 41, scale=3.0)
+    ref = ops.softmax_golden(parity.to_np(x).reshape(1, rows, cols), "f32", causal=causal)
+    ref = ref.reshape(rows, cols)
+    for shift in (0, 4):                                 # 4 floats = 16 bytes off
+        buf = torch.full((rows * cols + 8,), float("nan"), device=DEV)
+        out = buf[shift:shift + rows * cols]
+        assert (out.data_ptr() % 32 == 0) == (shift == 0)
+        _abi.call("fl_b200_softmax_lastdim", x.data_ptr(), cols, out.data_ptr(), cols, rows, cols,
+                  _abi.BF16, _abi.F32, int(causal), rows, 0,
+                  torch.cuda.current_stream().cuda_stream)
+        parity.assert_rel(parity.to_np(out).reshape(rows, cols), ref, rtol=1e-5, atol=1e-30,
+                          what=f"shift {shift}")
+        assert torch.isnan(buf[:shift]).all() and torch.isnan(buf[shift + rows * cols:]).all()
+
+
 def test_softmax_infinities():
     x = torch.tensor([[float("-inf")] * 8, [0.0, float("-inf"), 1.0, float("-inf"), 2, 3, 4, 5],
                       [1.0, float("nan"), 2, 3, 4, 5, 6, 7], [float("inf"), 1, 2, 3, 4, 5, 6, 7]])

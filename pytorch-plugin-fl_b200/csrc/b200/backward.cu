@@ -28,8 +28,11 @@ namespace {
 // partial of its columns in registers; at the end the row slots of the CTA
 // are added in slot order and the CTA's partial row goes to the workspace.
 // A second kernel adds the partial rows in CTA order.  Both orders are
-// fixed, so dw does not depend on timing.
-constexpr int kBwdCtasPerSm = 4;
+// fixed, so dw does not depend on timing.  The next row's x and dy are
+// loaded while the current row is reduced and stored (two row buffers in
+// registers, 3 CTAs per SM): measured on B200, bf16 [65536, 4096] 5.73 vs
+// 5.44 TB/s with one buffer at 4 CTAs per SM.
+constexpr int kBwdCtasPerSm = 3;
 
 template <typename T, int TPR, int VPT, int BLOCK>
 __global__ void __launch_bounds__(BLOCK, (BLOCK <= 256 ? kBwdCtasPerSm : 1))
@@ -47,12 +50,8 @@ rms_norm_bwd_kernel(const T* __restrict__ dy, int64_t lddy, const T* __restrict_
   for (int i = 0; i < VPT; ++i)
 #pragma unroll
     for (int e = 0; e < VW; ++e) acc[i][e] = 0.f;
-
-  for (int64_t base = (int64_t)blockIdx.x * RPB; base < rows;
-       base += (int64_t)gridDim.x * RPB) {
-    const int64_t row = base + slot;
+  auto load = [&](int64_t row, uint4 (&xv)[VPT], uint4 (&gv)[VPT]) {
     const bool ok = row < rows;
-    uint4 xv[VPT], gv[VPT];
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = lane + i * TPR;
@@ -60,7 +59,15 @@ rms_norm_bwd_kernel(const T* __restrict__ dy, int64_t lddy, const T* __restrict_
       xv[i] = in ? ld_stream(x + row * ldx + (int64_t)vi * VW) : make_uint4(0, 0, 0, 0);
       gv[i] = in ? ld_stream(dy + row * lddy + (int64_t)vi * VW) : make_uint4(0, 0, 0, 0);
     }
-    // sum x^2 and sum (w dy) x in one pass
+  };
+  uint4 xv[VPT], gv[VPT];
+  int64_t base = (int64_t)blockIdx.x * RPB;
+  load(base + slot, xv, gv);
+  for (; base < rows; base += (int64_t)gridDim.x * RPB) {
+    const int64_t row = base + slot;
+    const bool ok = row < rows;
+    uint4 xn[VPT], gn[VPT];
+    load(base + (int64_t)gridDim.x * RPB + slot, xn, gn);  // the next row, in flight meanwhile
     float ss = 0.f, tx = 0.f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -78,7 +85,7 @@ rms_norm_bwd_kernel(const T* __restrict__ dy, int64_t lddy, const T* __restrict_
     ss = row_reduce<SumOp, TPR, BLOCK>(ss, red);
     tx = row_reduce<SumOp, TPR, BLOCK>(tx, red);
     const float r = 1.0f / sqrtf(ss / cols_f + eps);
-    const float m = tx * r / cols_f;  // mean of (w dy) n
+    const float m = tx * r / cols_f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = lane + i * TPR;
@@ -95,9 +102,13 @@ rms_norm_bwd_kernel(const T* __restrict__ dy, int64_t lddy, const T* __restrict_
       }
       st_stream(dx + row * lddx + (int64_t)vi * VW, pack<T>(o));
     }
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      xv[i] = xn[i];
+      gv[i] = gn[i];
+    }
   }
   if (partial == nullptr) return;
-  // Add the row slots in slot order (through shared memory), then store.
   float* out = partial + (int64_t)blockIdx.x * nvec * VW;
   if constexpr (RPB == 1) {
 #pragma unroll

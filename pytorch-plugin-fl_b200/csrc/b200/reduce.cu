@@ -147,9 +147,10 @@ __device__ __forceinline__ float pack_max_nan(const uint4& u) {
 // and the ordinal of the pack where it last rose: it rises where a pack's
 // max is larger, or NaN while the running max is a number; an equal value
 // never moves it (packs arrive in increasing index order, so the first stays).
-// Afterwards the winning pack is read again (from L2) and searched for its
-// first element equal to the max (or first NaN).  Same result as folding
-// element by element with first-index ties and NaN as the maximum.
+// The winning pack stays in registers (copied on the rare rise), and is
+// searched at the end for its first element equal to the max (or first
+// NaN).  Same result as folding element by element with first-index ties
+// and NaN as the maximum.
 template <typename T, int U>
 __device__ __forceinline__ ArgMaxAcc argmax_packs(const T* xr, int64_t p0, int64_t p1) {
   constexpr int VW = Elem<T>::kVec;
@@ -159,23 +160,27 @@ __device__ __forceinline__ ArgMaxAcc argmax_packs(const T* xr, int64_t p0, int64
   const T* base = xr + first * VW;
   float best = -INFINITY;
   int bestk = 0;  // a thread whose packs are all -inf keeps its first pack
+  uint4 w = make_uint4(0, 0, 0, 0);
   for (int k0 = 0; k0 < n; k0 += U) {
     const T* pk = base + (int64_t)k0 * kBlock * VW;
     uint4 v[U];
 #pragma unroll
     for (int k = 0; k < U; ++k)
       if (k0 + k < n) v[k] = ld_stream(pk + k * kBlock * VW);
+    if (k0 == 0) w = v[0];
 #pragma unroll
     for (int k = 0; k < U; ++k) {
       if (k0 + k < n) {
         const float nb = max_nan_f32(best, pack_max_nan<T>(v[k]));
         const bool rose = (nb != best) && (best == best);
-        bestk = rose ? k0 + k : bestk;
+        if (rose) {
+          bestk = k0 + k;
+          w = v[k];
+        }
         best = nb;
       }
     }
   }
-  const uint4 w = ld_stream(base + (int64_t)bestk * kBlock * VW);
   float f[VW];
   unpack<T>(w, f);
   const bool nan = best != best;

@@ -33,7 +33,7 @@ def _none16(dt):
 # ------------------------------------------------------------------ RMSNorm
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("shape", [(1, 8), (3, 7), (5, 96), (127, 4096), (16, 8192),
-                                   (33, 1000), (2, 65536 + 8), (4096, 512), (3, 2, 256)])
+                                   (33, 1000), (2, 65536 + 8), (4096, 512), (3, 2, 256), (4, 16384)])
 def test_rms_norm_backward(dtype, shape):
     x = rnd(shape, dtype, 60)
     w = rnd(shape[-1:], dtype, 61, scale=0.1, loc=1.0)

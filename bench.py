@@ -10,7 +10,8 @@ layers (the bytes moved are the same as with fresh activations per layer).
 
 Outputs ONE JSON line (rank 0):
   value     tokens/s of the whole job, inputs resident in HBM, device time
-            (CUDA events), max over ranks.
+            (CUDA events), max over ranks; the step is replayed as one CUDA
+            graph of its launch list (--no-graph: eager launches).
   e2e       the same metric through the reference-facing plugin API (flagos
             tensors, torch_fl.ops) with the hidden state copied from pinned
             host memory before and back after every step.
@@ -19,7 +20,8 @@ Outputs ONE JSON line (rank 0):
   gpu_eager_reference  the HF formulas on PyTorch's own CUDA kernels (what
             the reference's cuda route runs) on the same stack, N=1.
   per_op    achieved HBM GB/s of every kernel of the step (CUDA events
-            around each launch inside the timed region).
+            around each launch, in a second timed pass of the same steps
+            launched one by one).
   cpu_baseline  the reference's CPU path (HF formulas on torch CPU aten) on
             a bounded sample, rank 0 at N=1.
 
@@ -430,6 +432,8 @@ def main():
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--eager-layers", type=int, default=4)
     ap.add_argument("--no-op-configs", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time the headline with eager launches instead of a CUDA graph replay")
     ap.add_argument("--profile-case", choices=sorted(PROFILE_CASES),
                     help="run one small case of one op once on GPU 0 and exit (for ncu)")
     args = ap.parse_args()
@@ -495,15 +499,32 @@ def main():
         stack.run(stack.x0)
     barrier()
 
-    # timed region: device time with events on the launching stream
+    # The step's launch list captured once as a CUDA graph: a replay issues
+    # the same kernels on the same buffers without per-launch host work.
+    graph = None
+    if not args.no_graph:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            stack.run(stack.x0)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            stack.run(stack.x0)
+        for _ in range(args.warmup):
+            graph.replay()
+        barrier()
+    step = graph.replay if graph is not None else (lambda: stack.run(stack.x0))
+
+    # timed region (the headline): device time with events on the launching
+    # stream, max over ranks
     clocks = ClockSampler(local)
     clocks.start()
-    timer = EventTimer()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     start.record()
     for _ in range(args.steps):
-        out = stack.run(stack.x0, timer)
+        step()
     end.record()
     torch.cuda.synchronize()
     barrier()
@@ -511,6 +532,22 @@ def main():
     ms = sharding.max_over_ranks(start.elapsed_time(end), dev)
     ms_per_step = ms / args.steps
     value = args.tokens * args.steps / (ms / 1e3)
+
+    # Per-kernel durations: a second timed pass of the same steps launched
+    # one by one with CUDA events around every launch (the events would add
+    # their own cost to the headline, so they are kept out of it).
+    timer = EventTimer()
+    barrier()
+    pass_start, pass_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pass_start.record()
+    for _ in range(args.steps):
+        stack.run(stack.x0, timer)
+    pass_end.record()
+    torch.cuda.synchronize()
+    barrier()
+    timed_pass_ms = sharding.max_over_ranks(pass_start.elapsed_time(pass_end), dev) / args.steps
+    if graph is not None:
+        del graph  # release before the process group goes away
 
     kern_ms = timer.mean_ms()
     counts = timer.counts()
@@ -650,11 +687,14 @@ def main():
                        "heads": [HQ, HKV, HEAD], "rounding": args.rounding,
                        "fused_add_rms_norm": not args.no_fuse_add_norm,
                        "parallelism": f"rows/{world}",
+                       "launch": "CUDA graph replay of the step" if not args.no_graph
+                                 else "eager launches",
                        "l2": "inputs larger than L2 (every per-rank activation >= 256 MB)"},
             "hbm_gbs_step": round(stack_bytes(stack) * args.steps / (ms / 1e3) / 1e9, 1),
             "per_op": per_op, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_eager_reference": eager, "per_op_configs": per_op_configs,
             "gpu_launches": stack.launches_per_step() * args.steps,
+            "per_kernel_pass_ms_per_step": round(timed_pass_ms, 3),
             "clocks": clock_info, "correctness": check,
         }
         print(json.dumps(line))

@@ -817,6 +817,9 @@ PROFILE_CASES = {
     "softmax_f16": "softmax f16 [1, 32, 4096, 4096]",
     "argmax": "argmax bf16 [8192, 32000]",
     "sum_all": "full sum f32 [16384, 8192]",
+    "rms_norm_backward": "RMSNorm backward bf16 [16384, 4096] (dx and dw)",
+    "swiglu_backward": "SwiGLU backward bf16 [4096, 14336]",
+    "softmax_backward": "softmax backward bf16 [2, 32, 2048, 2048]",
 }
 
 
@@ -838,9 +841,23 @@ def profile_case(name):
     elif name == "argmax":
         x = torch.randn(8192, 32000, generator=g, device=dev).to(torch.bfloat16)
         fn = lambda: K.argmax_lastdim(x)  # noqa: E731
-    else:
+    elif name == "sum_all":
         x = torch.randn(16384, 8192, generator=g, device=dev)
         fn = lambda: K.sum_all(x)  # noqa: E731
+    elif name == "rms_norm_backward":
+        x = torch.randn(16384, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+        dy = torch.randn(16384, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+        w = (1 + 0.1 * torch.randn(HIDDEN, generator=g, device=dev)).to(torch.bfloat16)
+        fn = lambda: K.rms_norm_backward(dy, x, w, EPS)  # noqa: E731
+    elif name == "swiglu_backward":
+        gt, up, d = (torch.randn(4096, INTER, generator=g, device=dev).to(torch.bfloat16)
+                     for _ in range(3))
+        fn = lambda: K.swiglu_backward(d, gt, up)  # noqa: E731
+    else:
+        x = (3.0 * torch.randn(2, 32, 2048, 2048, generator=g, device=dev)).to(torch.bfloat16)
+        y = K.softmax(x)
+        dy = torch.randn(2, 32, 2048, 2048, generator=g, device=dev).to(torch.bfloat16)
+        fn = lambda: K.softmax_backward(dy, y)  # noqa: E731
     fn()
     torch.cuda.synchronize()
     fn()

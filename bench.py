@@ -754,7 +754,19 @@ def op_configs(dev, peak, reps=5):
               "mask applied in the kernel; masked keys not read")
         timed(f"softmax_{name}_f32_out", lambda: K.softmax(masked, out_dtype=torch.float32),
               2 * n + 4 * n, "half_to_float (HF softmax(dtype=float32))")
-        del lg, masked
+        del masked
+        # HF eager attention's tail (scale, [B, 1, L, L] additive mask with the
+        # dtype's lowest value, softmax in fp32, cast back) as one launch; the
+        # same chain as PyTorch CUDA ops for comparison
+        hf = torch.zeros(8, 1, L, L, dtype=dt, device=dev).masked_fill(
+            torch.triu(torch.ones(L, L, dtype=torch.bool, device=dev), 1), torch.finfo(dt).min)
+        sc = 128 ** -0.5
+        timed(f"masked_softmax_{name}", lambda: K.masked_softmax(lg, hf, sc), 4 * n + hf.numel() * 2,
+              "HF eager attention tail in one launch: x*scale + mask, softmax, cast")
+        timed(f"masked_softmax_{name}_torch_chain", lambda: torch.softmax(
+            lg * sc + hf, -1, dtype=torch.float32).to(dt), 4 * n + hf.numel() * 2,
+            "the same tail as 4 PyTorch CUDA ops (bytes: the fused op's)")
+        del lg, hf
     # config 4: reductions
     xf = torch.randn(65536, 8192, generator=g, device=dev)
     n = xf.numel()
@@ -820,6 +832,7 @@ PROFILE_CASES = {
     "rms_norm_backward": "RMSNorm backward bf16 [16384, 4096] (dx and dw)",
     "swiglu_backward": "SwiGLU backward bf16 [4096, 14336]",
     "softmax_backward": "softmax backward bf16 [2, 32, 2048, 2048]",
+    "masked_softmax": "scaled masked softmax bf16 [2, 32, 2048, 2048], HF mask [2, 1, 2048, 2048]",
 }
 
 
@@ -853,6 +866,12 @@ def profile_case(name):
         gt, up, d = (torch.randn(4096, INTER, generator=g, device=dev).to(torch.bfloat16)
                      for _ in range(3))
         fn = lambda: K.swiglu_backward(d, gt, up)  # noqa: E731
+    elif name == "masked_softmax":
+        x = (3.0 * torch.randn(2, 32, 2048, 2048, generator=g, device=dev)).to(torch.bfloat16)
+        m = torch.zeros(2, 1, 2048, 2048, dtype=torch.bfloat16, device=dev).masked_fill(
+            torch.triu(torch.ones(2048, 2048, dtype=torch.bool, device=dev), 1),
+            torch.finfo(torch.bfloat16).min)
+        fn = lambda: K.masked_softmax(x, m, 128 ** -0.5)  # noqa: E731
     else:
         x = (3.0 * torch.randn(2, 32, 2048, 2048, generator=g, device=dev)).to(torch.bfloat16)
         y = K.softmax(x)

@@ -187,6 +187,28 @@ FL_B200_API int fl_b200_softmax_lastdim(const void* x, int64_t ld_x, void* out,
                                         int out_dtype, int causal,
                                         int64_t q_len, int64_t causal_offset,
                                         fl_b200_stream_t stream);
+/* Scaled, additively masked softmax over the last dim: the tail of HF's     *
+ * eager attention (transformers models/qwen3/modeling_qwen3.py             *
+ * eager_attention_forward: `attn_weights * scaling + attention_mask`,      *
+ * softmax(dtype=float32), `.to(query.dtype)`; the reference runs it as     *
+ * mul.cu:28-52, add.cu:48-84, _to_copy copy_ops.cc:225-240 and _softmax    *
+ * register.cc:270-272 -> softmax.cc:14-40, one launch and one full-size    *
+ * temporary each).  x holds rows = B*heads*q_len rows of `cols` keys, row  *
+ * r = (b*heads + h)*q_len + i at x + r*ld_x.  mask (NULL: none) has x's     *
+ * dtype; its row for (b, h, i) starts at mask + b*mask_stride_b +          *
+ * h*mask_stride_h + i*mask_stride_q elements and is contiguous (stride 0   *
+ * broadcasts: HF's [B, 1, Q, K] mask has mask_stride_h = 0).  FUSED        *
+ * computes x*scale + mask in fp32; CHAIN rounds to in_dtype after the      *
+ * scale and after the add, as the two aten ops do.  out_dtype = in_dtype   *
+ * (the cast back fused) or F32.  A row whose keys are all masked with the  *
+ * lowest finite value comes out uniform, as in the reference.              */
+FL_B200_API int fl_b200_softmax_masked(const void* x, int64_t ld_x, const void* mask,
+                                       int64_t mask_stride_b, int64_t mask_stride_h,
+                                       int64_t mask_stride_q, void* out, int64_t ld_out,
+                                       int64_t rows, int64_t cols, int64_t heads,
+                                       int64_t q_len, float scale, int in_dtype,
+                                       int out_dtype, int rounding,
+                                       fl_b200_stream_t stream);
 /* Softmax along a middle dim: x viewed dense as [outer, n, inner], softmax  *
  * over n for every (outer, inner).  Used for _softmax with dim != -1.      */
 FL_B200_API int fl_b200_softmax_middim(const void* x, void* out, int64_t outer,
@@ -324,6 +346,15 @@ FL_B200_API int fl_b200_softmax_bwd(const void* dy, int64_t ld_dy, const void* y
                                     int64_t ld_y, void* dx, int64_t ld_dx, int64_t rows,
                                     int64_t cols, int in_dtype, int out_dtype,
                                     fl_b200_stream_t stream);
+/* The same times `scale`: the backward of fl_b200_softmax_masked with      *
+ * respect to x (dx = scale * y * (dy - sum(dy * y))); the mask's gradient  *
+ * is the unscaled product summed over the dims it broadcasts.  Replaces    *
+ * the chain's _softmax_backward_data followed by mul.cu:28-52.             */
+FL_B200_API int fl_b200_softmax_bwd_scaled(const void* dy, int64_t ld_dy, const void* y,
+                                           int64_t ld_y, void* dx, int64_t ld_dx,
+                                           int64_t rows, int64_t cols, float scale,
+                                           int in_dtype, int out_dtype,
+                                           fl_b200_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -229,6 +229,39 @@ def softmax_golden(x, out_dtype: str, causal: bool = False, offset: int = 0) -> 
         return round_to(e / s, out_dtype)
 
 
+def masked_logits_chain(x, mask, scale: float, dtype: str) -> np.ndarray:
+    """The logits HF's eager attention hands its softmax
+    (transformers models/qwen3/modeling_qwen3.py eager_attention_forward):
+    `attn_weights * scaling` (mul with a scalar, fp32 opmath, rounded to the
+    dtype: csrc/aten/backends/cuda/mul.cu:28-52), then `+ attention_mask`
+    (add.cu:48-84, rounded again).  mask None: the scale only."""
+    t = round_to(np.asarray(x, np.float32) * np.float32(scale), dtype)
+    if mask is not None:
+        t = round_to(t + np.asarray(mask, np.float32), dtype)
+    return t
+
+
+def masked_softmax_chain(x, mask, scale: float, dtype: str, out_dtype: str) -> np.ndarray:
+    """The whole tail op by op: the logits above, softmax(dtype=float32)
+    (rounded to fp32) and `.to(query.dtype)` (rounded again to out_dtype)."""
+    z = masked_logits_chain(x, mask, scale, dtype)
+    return round_to(softmax_golden(z, "f32"), out_dtype)
+
+
+def masked_softmax_golden(x, mask, scale: float, out_dtype: str) -> np.ndarray:
+    """The fused formula: logits x * scale + mask rounded once to fp32 (one
+    FMA; fp64 holds x * scale exactly, so this is the FMA's rounding up to a
+    double-rounding tie), then the softmax in fp64
+    with one rounding to out_dtype.  A row whose keys are all masked with the
+    lowest finite value is uniform, as the reference's softmax makes it; with
+    an f16 mask (-65504) the fp32 logits keep x * scale to 2^-8, so such a
+    row is the softmax of those quantised logits."""
+    z = np.asarray(x, np.float64) * float(np.float32(scale))
+    if mask is not None:
+        z = z + np.asarray(mask, np.float64)
+    return softmax_golden(z.astype(np.float32), out_dtype)
+
+
 def softmax_dim_golden(x, dim: int, out_dtype: str) -> np.ndarray:
     x64 = np.asarray(x, np.float64)
     mx = np.max(x64, axis=dim, keepdims=True)
@@ -332,11 +365,13 @@ def silu_bwd_golden(dout, x, dtype: str):
         return round_to(d64 * s * (1.0 + x64 * (1.0 - s)), dtype)
 
 
-def softmax_bwd_golden(dy, y, dtype: str):
-    """dx = y (dy - sum(dy y)) over the last dim."""
+def softmax_bwd_golden(dy, y, dtype: str, scale: float = 1.0):
+    """dx = scale y (dy - sum(dy y)) over the last dim (scale != 1: the
+    gradient of softmax(x * scale + mask) with respect to x)."""
     g64 = np.asarray(dy, np.float64)
     y64 = np.asarray(y, np.float64)
-    return round_to(y64 * (g64 - np.sum(g64 * y64, axis=-1, keepdims=True)), dtype)
+    return round_to(float(scale) * y64 * (g64 - np.sum(g64 * y64, axis=-1, keepdims=True)),
+                    dtype)
 
 
 def softmax_bwd_bound(dy, y) -> np.ndarray:

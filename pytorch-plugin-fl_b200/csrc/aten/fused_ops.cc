@@ -1,6 +1,6 @@
 // flagos:: fused ops -- the kernels the HF hooks call in place of the
 // HuggingFace formulas (transformers models/qwen3/modeling_qwen3.py:59-64,
-// 81-82, 138-181, 248-268).  Registered for the flagos device and for plain
+// 81-82, 138-181, 209-213, 248-268).  Registered for the flagos device and for plain
 // CUDA tensors (the memory is the same kind); each op allocates its outputs
 // on the input's device and launches on that device's current stream.
 #include <torch/library.h>
@@ -223,6 +223,48 @@ at::Tensor CausalSoftmax(const at::Tensor& x_in, int64_t offset, std::optional<a
   return out;
 }
 
+// ---------------------------------------------------- masked softmax --
+// HF eager attention's `softmax(w * scaling + mask, dtype=float32)
+// .to(query.dtype)` (modeling_qwen3.py eager_attention_forward) in one
+// launch.  x is [B, H, Q, K] (or fewer leading dims); the mask has x's dtype
+// and broadcasts to x (HF's is [B, 1, Q, K]).
+at::Tensor MaskedSoftmax(const at::Tensor& x_in, const std::optional<at::Tensor>& mask_in,
+                         double scale, std::optional<at::ScalarType> dtype,
+                         c10::string_view rounding) {
+  const char* op = "flagos::masked_softmax";
+  const int ci = FloatCode(x_in, op);
+  const at::ScalarType ot = dtype.value_or(x_in.scalar_type());
+  const int co = B200Dtype(ot);
+  TORCH_CHECK(co == ci || co == FL_B200_F32, op, ": output dtype must be the input's or float32");
+  TORCH_CHECK(x_in.dim() >= 2 && x_in.dim() <= 4, op,
+              ": x must be [Q, K], [H, Q, K] or [B, H, Q, K]");
+  at::Tensor x4 = x_in;
+  while (x4.dim() < 4) x4 = x4.unsqueeze(0);
+  const int64_t H = x4.size(1), Q = x4.size(2), K = x4.size(3);
+  at::Tensor x;
+  const RowsView r = Rows(x4, x);
+  at::Tensor mask;
+  int64_t sb = 0, sh = 0, sq = 0;
+  if (mask_in.has_value() && mask_in->defined()) {
+    SameDevice(x_in, *mask_in, op);
+    TORCH_CHECK(mask_in->scalar_type() == x_in.scalar_type(), op, ": mask must have x's dtype, got ",
+                mask_in->scalar_type());
+    mask = mask_in->expand(x4.sizes());
+    if (K > 1 && mask.stride(3) != 1) mask = mask.contiguous();
+    sb = mask.stride(0);
+    sh = mask.stride(1);
+    sq = mask.stride(2);
+  }
+  at::Tensor out = at::empty(x4.sizes(), x.options().dtype(ot));
+  if (out.numel() == 0) return out.view(x_in.sizes());
+  GpuGuard g(x);
+  CheckB200(fl_b200_softmax_masked(x.data_ptr(), r.ld, mask.defined() ? mask.data_ptr() : nullptr,
+                                   sb, sh, sq, out.data_ptr(), K, r.rows, K, H, Q, (float)scale,
+                                   ci, co, Rounding(rounding), StreamOf(x)),
+            op);
+  return out.view(x_in.sizes());
+}
+
 // -------------------------------------------------------------- backward --
 // The backward ops the autograd formulas of the fused ops call
 // (torch_fl/autograd.py).  fp32 math, one rounding to the output dtype.
@@ -273,7 +315,7 @@ std::tuple<at::Tensor, at::Tensor> SwigluBackward(const at::Tensor& dout, const 
 }
 
 at::Tensor SoftmaxBackward(const at::Tensor& dy_in, const at::Tensor& y_in,
-                           std::optional<at::ScalarType> dtype) {
+                           std::optional<at::ScalarType> dtype, double scale) {
   const char* op = "flagos::softmax_backward";
   const int ci = FloatCode(y_in, op);
   SameDevice(y_in, dy_in, op);
@@ -287,8 +329,8 @@ at::Tensor SoftmaxBackward(const at::Tensor& dy_in, const at::Tensor& y_in,
   const RowsView r = Rows(y_in, y), rd = Rows(dy_in, dy);
   at::Tensor dx = at::empty(y.sizes(), y.options().dtype(ot));
   GpuGuard g(y);
-  CheckB200(fl_b200_softmax_bwd(dy.data_ptr(), rd.ld, y.data_ptr(), r.ld, dx.data_ptr(), r.cols,
-                                r.rows, r.cols, ci, co, StreamOf(y)),
+  CheckB200(fl_b200_softmax_bwd_scaled(dy.data_ptr(), rd.ld, y.data_ptr(), r.ld, dx.data_ptr(),
+                                       r.cols, r.rows, r.cols, (float)scale, ci, co, StreamOf(y)),
             op);
   return dx;
 }
@@ -309,7 +351,9 @@ TORCH_LIBRARY(flagos, m) {
   m.def("causal_softmax(Tensor x, int offset=0, ScalarType? dtype=None) -> Tensor");
   m.def("rms_norm_backward(Tensor dy, Tensor x, Tensor weight, float eps) -> (Tensor, Tensor)");
   m.def("swiglu_backward(Tensor dout, Tensor gate, Tensor up) -> (Tensor, Tensor)");
-  m.def("softmax_backward(Tensor dy, Tensor y, ScalarType? dtype=None) -> Tensor");
+  m.def("softmax_backward(Tensor dy, Tensor y, ScalarType? dtype=None, float scale=1.0) -> Tensor");
+  m.def("masked_softmax(Tensor x, Tensor? mask=None, float scale=1.0, ScalarType? dtype=None, "
+        "str rounding='fused') -> Tensor");
 }
 
 #define FLB_FUSED_IMPLS(m)                          \
@@ -322,7 +366,8 @@ TORCH_LIBRARY(flagos, m) {
   m.impl("causal_softmax", CausalSoftmax);          \
   m.impl("rms_norm_backward", RmsNormBackward);     \
   m.impl("swiglu_backward", SwigluBackward);        \
-  m.impl("softmax_backward", SoftmaxBackward);
+  m.impl("softmax_backward", SoftmaxBackward);      \
+  m.impl("masked_softmax", MaskedSoftmax);
 
 TORCH_LIBRARY_IMPL(flagos, PrivateUse1, m) { FLB_FUSED_IMPLS(m) }
 TORCH_LIBRARY_IMPL(flagos, CUDA, m) { FLB_FUSED_IMPLS(m) }

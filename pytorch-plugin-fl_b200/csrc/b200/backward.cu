@@ -331,7 +331,7 @@ template <typename TI, typename TO, int TPR, int VPT, int BLOCK>
 __global__ void __launch_bounds__(BLOCK, ladder_min_blocks<BLOCK>())
 softmax_bwd_vec_kernel(const TI* __restrict__ dy, int64_t lddy, const TI* __restrict__ y,
                        int64_t ldy, TO* __restrict__ dx, int64_t lddx, int64_t rows,
-                       int nvec) {
+                       int nvec, float scale) {
   constexpr int VW = Elem<TI>::kVec;
   constexpr int RPB = BLOCK / TPR;
   __shared__ float red[BLOCK / 32];
@@ -367,7 +367,7 @@ softmax_bwd_vec_kernel(const TI* __restrict__ dy, int64_t lddy, const TI* __rest
       unpack<TI>(opaque(gv[i]), gf);
       unpack<TI>(opaque(yv[i]), yf);
 #pragma unroll
-      for (int e = 0; e < VW; ++e) o[e] = yf[e] * (gf[e] - dot);
+      for (int e = 0; e < VW; ++e) o[e] = yf[e] * (gf[e] - dot) * scale;
       TO* dst = dx + row * lddx + (int64_t)vi * VW;
       if constexpr (Elem<TO>::kVec <= VW) {
         store_vals_bwd<TO, VW>(dst, o);
@@ -386,7 +386,7 @@ softmax_bwd_vec_kernel(const TI* __restrict__ dy, int64_t lddy, const TI* __rest
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(256)
 softmax_bwd_loop_kernel(const TI* dy, int64_t lddy, const TI* y, int64_t ldy, TO* dx,
-                        int64_t lddx, int64_t rows, int64_t cols) {
+                        int64_t lddx, int64_t rows, int64_t cols, float scale) {
   __shared__ float red[256 / 32];
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const TI* gr = dy + row * lddy;
@@ -396,7 +396,7 @@ softmax_bwd_loop_kernel(const TI* dy, int64_t lddy, const TI* y, int64_t ldy, TO
       dot = fmaf(Elem<TI>::to_f(gr[c]), Elem<TI>::to_f(yr[c]), dot);
     dot = block_reduce<SumOp, 256>(dot, red);
     for (int64_t c = threadIdx.x; c < cols; c += 256) {
-      const float v = Elem<TI>::to_f(yr[c]) * (Elem<TI>::to_f(gr[c]) - dot);
+      const float v = Elem<TI>::to_f(yr[c]) * (Elem<TI>::to_f(gr[c]) - dot) * scale;
       if constexpr (std::is_same<TO, float>::value) dx[row * lddx + c] = v;
       else dx[row * lddx + c] = Elem<TO>::from_f(v);
     }
@@ -405,7 +405,8 @@ softmax_bwd_loop_kernel(const TI* dy, int64_t lddy, const TI* y, int64_t ldy, TO
 
 template <typename TI, typename TO>
 int launch_softmax_bwd(const TI* dy, int64_t lddy, const TI* y, int64_t ldy, TO* dx,
-                       int64_t lddx, int64_t rows, int64_t cols, cudaStream_t stream) {
+                       int64_t lddx, int64_t rows, int64_t cols, float scale,
+                       cudaStream_t stream) {
   DeviceInfo dev;
   int st = current_device_info(&dev);
   if (st != FL_B200_OK) return st;
@@ -423,7 +424,7 @@ int launch_softmax_bwd(const TI* dy, int64_t lddy, const TI* y, int64_t ldy, TO*
       constexpr int BLOCK = ladder_block<TPR>();
       softmax_bwd_vec_kernel<TI, TO, TPR, VPT, BLOCK>
           <<<full_grid(ceil_div(rows, BLOCK / TPR)), BLOCK, 0, stream>>>(
-              dy, lddy, y, ldy, dx, lddx, rows, (int)(cols / VW));
+              dy, lddy, y, ldy, dx, lddx, rows, (int)(cols / VW), scale);
       return launch_status();
     });
     if (r >= 0) return r;
@@ -431,7 +432,7 @@ int launch_softmax_bwd(const TI* dy, int64_t lddy, const TI* y, int64_t ldy, TO*
   auto kern = softmax_bwd_loop_kernel<TI, TO>;
   static const int per_sm = blocks_per_sm(kern, 256, 0);
   const int grid = (int)std::min<int64_t>(rows, (int64_t)per_sm * dev.sm_count);
-  kern<<<grid, 256, 0, stream>>>(dy, lddy, y, ldy, dx, lddx, rows, cols);
+  kern<<<grid, 256, 0, stream>>>(dy, lddy, y, ldy, dx, lddx, rows, cols, scale);
   return launch_status();
 }
 
@@ -512,10 +513,11 @@ FL_B200_API int fl_b200_silu_bwd(const void* dout, const void* x, void* dx, int6
   });
 }
 
-FL_B200_API int fl_b200_softmax_bwd(const void* dy, int64_t ld_dy, const void* y,
-                                    int64_t ld_y, void* dx, int64_t ld_dx, int64_t rows,
-                                    int64_t cols, int in_dtype, int out_dtype,
-                                    fl_b200_stream_t stream) {
+FL_B200_API int fl_b200_softmax_bwd_scaled(const void* dy, int64_t ld_dy, const void* y,
+                                           int64_t ld_y, void* dx, int64_t ld_dx,
+                                           int64_t rows, int64_t cols, float scale,
+                                           int in_dtype, int out_dtype,
+                                           fl_b200_stream_t stream) {
   using namespace flb200;
   FLB_CHECK_ARG(rows >= 0 && cols >= 0);
   if (rows == 0 || cols == 0) return FL_B200_OK;
@@ -526,12 +528,20 @@ FL_B200_API int fl_b200_softmax_bwd(const void* dy, int64_t ld_dy, const void* y
     using TO = decltype(to);
     return launch_softmax_bwd<TI, TO>(static_cast<const TI*>(dy), ld_dy,
                                       static_cast<const TI*>(y), ld_y, static_cast<TO*>(dx),
-                                      ld_dx, rows, cols, s);
+                                      ld_dx, rows, cols, scale, s);
   };
   if (in_dtype == out_dtype) return dispatch_float(in_dtype, [&](auto t) { return go(t, t); });
   if (in_dtype == FL_B200_F32 && out_dtype == FL_B200_BF16) return go(float{}, __nv_bfloat16{});
   if (in_dtype == FL_B200_F32 && out_dtype == FL_B200_F16) return go(float{}, __half{});
   return FL_B200_ERR_UNSUPPORTED_DTYPE;
+}
+
+FL_B200_API int fl_b200_softmax_bwd(const void* dy, int64_t ld_dy, const void* y,
+                                    int64_t ld_y, void* dx, int64_t ld_dx, int64_t rows,
+                                    int64_t cols, int in_dtype, int out_dtype,
+                                    fl_b200_stream_t stream) {
+  return fl_b200_softmax_bwd_scaled(dy, ld_dy, y, ld_y, dx, ld_dx, rows, cols, 1.0f, in_dtype,
+                                    out_dtype, stream);
 }
 
 }  // extern "C"

@@ -6,8 +6,15 @@
 // causal variant applies the mask itself: masked keys are never read and are
 // written as exact zeros, so a causal row of L keys costs (i+1)/L of a read.
 //
-// exp(x - m) is evaluated as exp2f(x*log2e - m*log2e) with one FMA; the row
-// stays in registers (row_ladder), so HBM sees one read and one write.
+// exp(x - m) is evaluated as exp2f(x*log2e - m*log2e) with one FMA (rows
+// whose max is too far below zero for that are shifted by it first, exactly,
+// wide_max); the row stays in registers (row_ladder), so HBM sees one read
+// and one write.
+//
+// softmax_masked is HF's eager-attention tail in one pass
+// (modeling_qwen3.py eager_attention_forward: `w * scaling + mask`,
+// softmax(dtype=float32), `.to(query.dtype)`): scale, additive mask
+// broadcast over heads, softmax, and the cast of the result.
 #include "row_ladder.cuh"
 
 namespace flb200 {
@@ -28,6 +35,39 @@ __device__ __forceinline__ float ex2_approx(float t) {
 __device__ __forceinline__ float exp_shifted(float x, float mlog2e) {
   return ex2_approx(fmaf(x, kLog2e, -mlog2e));
 }
+
+// A row max too far below zero for the one-FMA exp: m*log2e overflows to
+// -inf for a finite m below -2.36e38, e.g. a row whose every key is masked
+// with the lowest finite value (HF's additive attention mask for a padding
+// query).  Every key x of such a row lies in [-3.41e38, m], within a factor
+// of 2 of m, so x - m is exact in the row's own format (Sterbenz's lemma):
+// the register-resident kernels subtract m from their packs once (a
+// row-uniform branch that ordinary rows never take) and continue with m = 0,
+// so the row comes out uniform over its keys as in the reference, not NaN.
+__device__ __forceinline__ bool wide_max(float m) {
+  return m * kLog2e == -INFINITY && m != -INFINITY;
+}
+template <typename T>
+__device__ __forceinline__ uint4 shift_pack(const uint4& v, float m) {
+  constexpr int VW = Elem<T>::kVec;
+  float f[VW];
+  unpack<T>(v, f);
+#pragma unroll
+  for (int e = 0; e < VW; ++e) f[e] -= m;
+  return pack<T>(f);
+}
+
+// The same for the looped kernels, which read the row again instead of
+// keeping it: exp(x - m) in the one-FMA form, or x - m first for a wide row.
+struct RowShift {
+  float m, ml;
+  bool wide;
+  __device__ __forceinline__ explicit RowShift(float row_max)
+      : m(row_max), ml(row_max * kLog2e), wide(wide_max(row_max)) {}
+  __device__ __forceinline__ float exp(float x) const {
+    return wide ? ex2_approx((x - m) * kLog2e) : exp_shifted(x, ml);
+  }
+};
 
 // Max of a 16-byte pack as fp32, NaN ignored like fmaxf (a NaN anywhere in
 // the row still makes every output NaN through its exp).  16-bit packs use
@@ -260,6 +300,15 @@ softmax_vec_kernel(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
     if constexpr (CAUSAL) with_count<0, VPT, STEP>(iters, load_max);
     else load_max(Full{});
     m = row_reduce<FastMaxOp, TPR, BLOCK>(m, smem);
+    if (wide_max(m)) {
+      const auto shift = [&](auto kc) {
+#pragma unroll
+        for (int i = 0; i < decltype(kc)::value; ++i) v[i] = shift_pack<TI>(v[i], m);
+      };
+      if constexpr (CAUSAL) with_count<0, VPT, STEP>(iters, shift);
+      else shift(Full{});
+      m = 0.f;
+    }
     if constexpr (CAUSAL) with_count<0, VPT, STEP>(iters, exp_sum);
     else exp_sum(Full{});
     s = row_reduce<SumOp, TPR, BLOCK>(s, smem);
@@ -294,11 +343,11 @@ softmax_loop_kernel(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
     const float part = (m == -INFINITY) ? 0.f : s * exp2f((m - mrow) * kLog2e);
     const float srow = block_reduce<SumOp, 256>(part, smem);
     const float inv = nvalid > 0 ? 1.0f / srow : __int_as_float(0x7fc00000);
-    const float ml = mrow * kLog2e;
+    const RowShift sh(mrow);
     TO* yr = y + row * ldy;
     for (int64_t c = threadIdx.x; c < cols; c += 256) {
       float o;
-      if (c < nvalid) o = exp_shifted(Elem<TI>::to_f(xr[c]), ml) * inv;
+      if (c < nvalid) o = sh.exp(Elem<TI>::to_f(xr[c])) * inv;
       else o = nvalid > 0 ? 0.f : inv;
       if constexpr (std::is_same<TO, float>::value) yr[c] = o;
       else yr[c] = Elem<TO>::from_f(o);
@@ -319,12 +368,12 @@ softmax_middim_kernel(const TI* x, TO* y, int64_t outer, int64_t n, int64_t inne
     TO* yc = y + o * n * inner + in;
     float m = -INFINITY;
     for (int64_t k = 0; k < n; ++k) m = fmaxf(m, Elem<TI>::to_f(xc[k * inner]));
-    const float ml = m * kLog2e;
+    const RowShift sh(m);
     float s = 0.f;
-    for (int64_t k = 0; k < n; ++k) s += exp_shifted(Elem<TI>::to_f(xc[k * inner]), ml);
+    for (int64_t k = 0; k < n; ++k) s += sh.exp(Elem<TI>::to_f(xc[k * inner]));
     const float inv = 1.0f / s;
     for (int64_t k = 0; k < n; ++k) {
-      const float v = exp_shifted(Elem<TI>::to_f(xc[k * inner]), ml) * inv;
+      const float v = sh.exp(Elem<TI>::to_f(xc[k * inner])) * inv;
       if constexpr (std::is_same<TO, float>::value) yc[k * inner] = v;
       else yc[k * inner] = Elem<TO>::from_f(v);
     }
@@ -373,6 +422,181 @@ int launch_softmax(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
   return launch_status();
 }
 
+// ------------------------------------------------------- masked softmax ---
+// Row r of x (viewed [B, H, Q, K]) is query i = r % Q of head h = (r / Q) % H
+// in batch b = r / (Q*H); its mask row starts at b*sb + h*sh + i*sq elements
+// (a stride of 0 broadcasts, e.g. HF's [B, 1, Q, K] mask over the heads).
+struct MaskRows {
+  int64_t heads, q_len, sb, sh, sq;
+  __device__ __forceinline__ int64_t offset(int64_t row) const {
+    const int64_t i = row % q_len, t = row / q_len;
+    return (t / heads) * sb + (t % heads) * sh + i * sq;
+  }
+};
+
+// The logit the softmax sees: x*scale + mask.  FUSED: one fp32 FMA.  CHAIN:
+// rounded to T after the scale and after the mask add, as HF's two aten ops
+// (mul by the scalar, add of the mask) leave it; no FMA contraction.
+template <typename T, bool MASK, bool CHAIN>
+__device__ __forceinline__ float masked_logit(float x, float scale, float mk) {
+  if constexpr (CHAIN) {
+    const float t = round_to<T>(__fmul_rn(x, scale));
+    return MASK ? round_to<T>(__fadd_rn(t, mk)) : t;
+  } else {
+    return MASK ? fmaf(x, scale, mk) : x * scale;
+  }
+}
+
+// Rows in registers as fp32 logits: x and mask packs are loaded together,
+// turned into logits, max, exps in place, sum, one store pass.  The mask is
+// read through L2: the rows of one batch's heads are scheduled together, so
+// a [B, 1, Q, K] mask comes from DRAM about once per batch.
+template <typename TI, typename TO, int TPR, int VPT, int BLOCK, bool MASK, bool CHAIN, bool W32>
+__global__ void __launch_bounds__(BLOCK, ladder_min_blocks<BLOCK>())
+softmax_masked_kernel(const TI* __restrict__ x, int64_t ldx, const TI* __restrict__ mask,
+                      MaskRows mg, TO* __restrict__ y, int64_t ldy, int64_t rows, int nvec,
+                      float scale) {
+  constexpr int VW = Elem<TI>::kVec;
+  constexpr int RPB = BLOCK / TPR;
+  __shared__ float smem[BLOCK / 32];
+  const int slot = threadIdx.x / TPR;
+  const int lane = threadIdx.x % TPR;
+  for (int64_t base = (int64_t)blockIdx.x * RPB; base < rows;
+       base += (int64_t)gridDim.x * RPB) {
+    const int64_t row = base + slot;
+    const bool ok = row < rows;
+    const TI* xr = x + row * ldx;
+    const TI* mr = MASK ? mask + mg.offset(ok ? row : 0) : nullptr;
+    uint4 xv[VPT], mv[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = lane + i * TPR;
+      const bool in = ok && vi < nvec;
+      xv[i] = in ? ld_stream(xr + (int64_t)vi * VW) : make_uint4(0, 0, 0, 0);
+      if constexpr (MASK) mv[i] = in ? ld_stream(mr + (int64_t)vi * VW) : make_uint4(0, 0, 0, 0);
+    }
+    float v[VPT][VW];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const bool in = ok && lane + i * TPR < nvec;
+      float f[VW], mk[VW];
+      unpack<TI>(xv[i], f);
+      if constexpr (MASK) unpack<TI>(mv[i], mk);
+#pragma unroll
+      for (int e = 0; e < VW; ++e) {
+        v[i][e] = in ? masked_logit<TI, MASK, CHAIN>(f[e], scale, MASK ? mk[e] : 0.f) : -INFINITY;
+        m = fmaxf(m, v[i][e]);
+      }
+    }
+    m = row_reduce<FastMaxOp, TPR, BLOCK>(m, smem);
+    if (wide_max(m)) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+#pragma unroll
+        for (int e = 0; e < VW; ++e) v[i][e] -= m;
+      m = 0.f;
+    }
+    const float ml = m * kLog2e;
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+#pragma unroll
+      for (int e = 0; e < VW; ++e) v[i][e] = exp_shifted(v[i][e], ml);
+      float t[VW];
+#pragma unroll
+      for (int e = 0; e < VW; ++e) t[e] = v[i][e];
+#pragma unroll
+      for (int w = VW / 2; w >= 1; w /= 2)
+#pragma unroll
+        for (int e = 0; e < w; ++e) t[e] += t[e + w];
+      s += t[0];
+    }
+    s = row_reduce<SumOp, TPR, BLOCK>(s, smem);
+    const float inv = 1.0f / s;
+    TO* yr = y + row * ldy;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = lane + i * TPR;
+      if (!ok || vi >= nvec) continue;
+      float o[VW];
+#pragma unroll
+      for (int e = 0; e < VW; ++e) o[e] = v[i][e] * inv;
+      store_vals<TO, VW, W32>(yr + (int64_t)vi * VW, o);
+    }
+  }
+}
+
+// Any row length / alignment: one CTA per row, three passes over the row
+// (the second and third mostly from L2).
+template <typename TI, typename TO, bool MASK, bool CHAIN>
+__global__ void __launch_bounds__(256)
+softmax_masked_loop_kernel(const TI* x, int64_t ldx, const TI* mask, MaskRows mg, TO* y,
+                           int64_t ldy, int64_t rows, int64_t cols, float scale) {
+  __shared__ float smem[256 / 32];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const TI* xr = x + row * ldx;
+    const TI* mr = MASK ? mask + mg.offset(row) : nullptr;
+    const auto logit = [&](int64_t c) {
+      return masked_logit<TI, MASK, CHAIN>(Elem<TI>::to_f(xr[c]), scale,
+                                           MASK ? Elem<TI>::to_f(mr[c]) : 0.f);
+    };
+    float m = -INFINITY;
+    for (int64_t c = threadIdx.x; c < cols; c += 256) m = fmaxf(m, logit(c));
+    m = block_reduce<FastMaxOp, 256>(m, smem);
+    const RowShift sh(m);
+    float s = 0.f;
+    for (int64_t c = threadIdx.x; c < cols; c += 256) s += sh.exp(logit(c));
+    s = block_reduce<SumOp, 256>(s, smem);
+    const float inv = 1.0f / s;
+    TO* yr = y + row * ldy;
+    for (int64_t c = threadIdx.x; c < cols; c += 256) {
+      const float o = sh.exp(logit(c)) * inv;
+      if constexpr (std::is_same<TO, float>::value) yr[c] = o;
+      else yr[c] = Elem<TO>::from_f(o);
+    }
+  }
+}
+
+template <typename TI, typename TO, bool MASK, bool CHAIN>
+int launch_softmax_masked(const TI* x, int64_t ldx, const TI* mask, const MaskRows& mg, TO* y,
+                          int64_t ldy, int64_t rows, int64_t cols, float scale,
+                          cudaStream_t stream) {
+  DeviceInfo dev;
+  int st = current_device_info(&dev);
+  if (st != FL_B200_OK) return st;
+  constexpr int VW = Elem<TI>::kVec;
+  const bool mask_ok = !MASK || (aligned16(mask) && mg.sb % VW == 0 && mg.sh % VW == 0 &&
+                                 mg.sq % VW == 0);
+  const bool vec_ok = mask_ok && aligned16(x) && aligned16(y) && cols % VW == 0 &&
+                      ldx % VW == 0 && ldy % VW == 0;
+  if (vec_ok) {
+    const int r = row_ladder<8>(cols / VW, [&](auto tpr, auto vpt) -> int {
+      constexpr int TPR = decltype(tpr)::value;
+      constexpr int VPT = decltype(vpt)::value;
+      constexpr int BLOCK = ladder_block<TPR>();
+      const int grid = full_grid(ceil_div(rows, BLOCK / TPR));
+      if constexpr (std::is_same<TO, float>::value && VW == 8) {
+        if (aligned32(y) && ldy % 8 == 0) {
+          softmax_masked_kernel<TI, TO, TPR, VPT, BLOCK, MASK, CHAIN, true>
+              <<<grid, BLOCK, 0, stream>>>(x, ldx, mask, mg, y, ldy, rows, (int)(cols / VW),
+                                           scale);
+          return launch_status();
+        }
+      }
+      softmax_masked_kernel<TI, TO, TPR, VPT, BLOCK, MASK, CHAIN, false>
+          <<<grid, BLOCK, 0, stream>>>(x, ldx, mask, mg, y, ldy, rows, (int)(cols / VW), scale);
+      return launch_status();
+    });
+    if (r >= 0) return r;
+  }
+  auto kern = softmax_masked_loop_kernel<TI, TO, MASK, CHAIN>;
+  static const int per_sm = blocks_per_sm(kern, 256, 0);
+  const int grid = (int)std::min<int64_t>(rows, (int64_t)per_sm * dev.sm_count);
+  kern<<<grid, 256, 0, stream>>>(x, ldx, mask, mg, y, ldy, rows, cols, scale);
+  return launch_status();
+}
+
 // Calls f(TI{}, TO{}) for the supported (in, out) pairs: out == in, or
 // 16-bit in with fp32 out (half_to_float).
 template <typename F>
@@ -412,6 +636,41 @@ FL_B200_API int fl_b200_softmax_lastdim(const void* x, int64_t ld_x, void* out,
       return launch_softmax<TI, TO, true>(xp, ld_x, yp, ld_out, rows, cols, q_len,
                                           causal_offset, s);
     return launch_softmax<TI, TO, false>(xp, ld_x, yp, ld_out, rows, cols, 1, 0, s);
+  });
+}
+
+FL_B200_API int fl_b200_softmax_masked(const void* x, int64_t ld_x, const void* mask,
+                                       int64_t mask_stride_b, int64_t mask_stride_h,
+                                       int64_t mask_stride_q, void* out, int64_t ld_out,
+                                       int64_t rows, int64_t cols, int64_t heads,
+                                       int64_t q_len, float scale, int in_dtype,
+                                       int out_dtype, int rounding,
+                                       fl_b200_stream_t stream) {
+  using namespace flb200;
+  FLB_CHECK_ARG(rows >= 0 && cols >= 0 && heads > 0 && q_len > 0);
+  FLB_CHECK_ARG(rows % (heads * q_len) == 0);
+  FLB_CHECK_ARG(rounding == FL_B200_ROUND_FUSED || rounding == FL_B200_ROUND_CHAIN);
+  if (rows == 0 || cols == 0) return FL_B200_OK;
+  FLB_CHECK_ARG(x && out && ld_x >= cols && ld_out >= cols);
+  const MaskRows mg{heads, q_len, mask_stride_b, mask_stride_h, mask_stride_q};
+  auto s = static_cast<cudaStream_t>(stream);
+  return dispatch_in_out(in_dtype, out_dtype, [&](auto ti, auto to) -> int {
+    using TI = decltype(ti);
+    using TO = decltype(to);
+    auto xp = static_cast<const TI*>(x);
+    auto mp = static_cast<const TI*>(mask);
+    auto yp = static_cast<TO*>(out);
+    const bool chain = rounding == FL_B200_ROUND_CHAIN;
+    if (mask) {
+      return chain ? launch_softmax_masked<TI, TO, true, true>(xp, ld_x, mp, mg, yp, ld_out, rows,
+                                                                cols, scale, s)
+                   : launch_softmax_masked<TI, TO, true, false>(xp, ld_x, mp, mg, yp, ld_out,
+                                                                 rows, cols, scale, s);
+    }
+    return chain ? launch_softmax_masked<TI, TO, false, true>(xp, ld_x, mp, mg, yp, ld_out, rows,
+                                                               cols, scale, s)
+                 : launch_softmax_masked<TI, TO, false, false>(xp, ld_x, mp, mg, yp, ld_out,
+                                                                rows, cols, scale, s);
   });
 }
 

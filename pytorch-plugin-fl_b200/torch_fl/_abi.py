@@ -55,6 +55,9 @@ PROTOTYPES: dict[str, tuple] = {
     "fl_b200_softmax_lastdim": (
         _i32, [_p, _i64, _p, _i64, _i64, _i64, _i32, _i32, _i32, _i64, _i64, _p]),
     "fl_b200_softmax_middim": (_i32, [_p, _p, _i64, _i64, _i64, _i32, _i32, _p]),
+    "fl_b200_softmax_masked": (
+        _i32, [_p, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _f32,
+               _i32, _i32, _i32, _p]),
     "fl_b200_reduce_workspace_size": (_sz, [_i64, _i64]),
     "fl_b200_reduce_sum_lastdim": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _i32, _p, _sz, _p]),
     "fl_b200_reduce_mean_lastdim": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _i32, _p, _sz, _p]),
@@ -72,6 +75,8 @@ PROTOTYPES: dict[str, tuple] = {
     "fl_b200_swiglu_bwd": (_i32, [_p, _p, _p, _p, _p, _i64, _i32, _p]),
     "fl_b200_silu_bwd": (_i32, [_p, _p, _p, _i64, _i32, _p]),
     "fl_b200_softmax_bwd": (_i32, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i32, _i32, _p]),
+    "fl_b200_softmax_bwd_scaled": (
+        _i32, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _f32, _i32, _i32, _p]),
 }
 
 

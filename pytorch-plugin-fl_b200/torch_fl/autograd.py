@@ -19,6 +19,9 @@ rounding the forward used.
                     d(x) = d(y) = d_h
 * causal_softmax(x): dx = softmax_backward(dy, y, x.dtype) (masked keys have
   y = 0, so their gradient is 0)
+* masked_softmax(x, mask, scale): dx = softmax_backward(dy, y, x.dtype, scale);
+  a mask that needs a gradient gets the unscaled product summed over the
+  dims it broadcasts (HF's mask needs none)
 """
 
 from __future__ import annotations
@@ -148,6 +151,25 @@ def _softmax_backward(ctx, dy):
     return dx if ctx.needs_input_grad[0] else None, None, None
 
 
+def _masked_softmax_setup(ctx, inputs, output):
+    x, mask, scale, _, _ = inputs
+    ctx.save_for_backward(output)
+    ctx.in_dtype = x.dtype
+    ctx.scale = scale
+    ctx.mask_meta = None if mask is None else (mask.shape, mask.dtype)
+
+
+def _masked_softmax_backward(ctx, dy):
+    (y,) = ctx.saved_tensors
+    dx = dmask = None
+    if ctx.needs_input_grad[0]:
+        dx = _F.softmax_backward(dy, y, ctx.in_dtype, ctx.scale)
+    if ctx.mask_meta is not None and ctx.needs_input_grad[1]:
+        shape, dtype = ctx.mask_meta
+        dmask = _F.softmax_backward(dy, y, None, 1.0).sum_to_size(shape).to(dtype)
+    return dx, dmask, None, None, None
+
+
 def register() -> None:
     """Attach the formulas to the flagos:: ops (once per process)."""
     reg = torch.library.register_autograd
@@ -158,3 +180,4 @@ def register() -> None:
     reg("flagos::swiglu", _swiglu_backward, setup_context=_swiglu_setup)
     reg("flagos::swiglu_residual", _swiglu_res_backward, setup_context=_swiglu_res_setup)
     reg("flagos::causal_softmax", _softmax_backward, setup_context=_softmax_setup)
+    reg("flagos::masked_softmax", _masked_softmax_backward, setup_context=_masked_softmax_setup)

@@ -6,12 +6,14 @@ aten op for the flagos device.
 
 `enable_hf_fused_ops()` is the site the reference lacks (it has no HF hooks):
 it replaces, in the installed transformers, the forward of the RMSNorm
-modules, the module-level `apply_rotary_pos_emb`, and the SwiGLU MLP forward
-of the Qwen3 / Qwen2 / Llama / Mistral model files with the flagos:: fused
-kernels.  The hooks act on device tensors (flagos or cuda), in inference and
+modules, the module-level `apply_rotary_pos_emb`, the SwiGLU MLP forward and
+the module-level `eager_attention_forward` (its scale + mask + softmax +
+cast tail becomes one flagos::masked_softmax launch; the two matmuls stay
+torch's) of the Qwen3 / Qwen2 / Llama / Mistral model files with the
+flagos:: fused kernels.  The hooks act on device tensors (flagos or cuda), in inference and
 in training (the fused ops carry autograd formulas, torch_fl/autograd.py);
-CPU tensors, and RoPE tables that themselves need a gradient, run the
-original HF code unchanged.  `disable_hf_fused_ops()` restores the originals.
+CPU tensors, RoPE tables that themselves need a gradient, and attention
+with dropout active, run the original HF code unchanged.  `disable_hf_fused_ops()` restores the originals.
 """
 
 from __future__ import annotations
@@ -100,6 +102,30 @@ def _mlp_forward(orig):
     return forward
 
 
+def _attention_fn(orig):
+    repeat_kv = getattr(importlib.import_module(orig.__module__), "repeat_kv", None)
+
+    def eager_attention_forward(module, query, key, value, attention_mask, scaling,
+                                dropout=0.0, **kwargs):
+        mask = attention_mask
+        mask_ok = mask is None or (_fusable(mask) and mask.dtype == query.dtype
+                                   and mask.dim() == 4 and mask.shape[-1] == key.shape[-2])
+        dropping = bool(dropout) and module.training
+        if (repeat_kv is None or dropping or not mask_ok or query.dim() != 4
+                or not _fusable(query, key, value)):
+            return orig(module, query, key, value, attention_mask, scaling, dropout, **kwargs)
+        groups = module.num_key_value_groups
+        key_states = repeat_kv(key, groups)
+        value_states = repeat_kv(value, groups)
+        w = torch.matmul(query, key_states.transpose(2, 3))
+        w = ops.masked_softmax(w, mask, float(scaling), None, _rounding)
+        out = torch.matmul(w, value_states).transpose(1, 2).contiguous()
+        return out, w
+
+    eager_attention_forward.__wrapped__ = orig
+    return eager_attention_forward
+
+
 def enable_hf_fused_ops(models=tuple(_MODEL_FILES), rounding: Optional[str] = None) -> list:
     """Patch the installed transformers model files; returns what was patched."""
     global _rounding
@@ -113,7 +139,8 @@ def enable_hf_fused_ops(models=tuple(_MODEL_FILES), rounding: Optional[str] = No
         norm_cls, mlp_cls = _MODEL_FILES[name]
         targets = [(getattr(mod, norm_cls, None), "forward", _rms_forward),
                    (getattr(mod, mlp_cls, None), "forward", _mlp_forward),
-                   (mod, "apply_rotary_pos_emb", _rope_fn)]
+                   (mod, "apply_rotary_pos_emb", _rope_fn),
+                   (mod, "eager_attention_forward", _attention_fn)]
         for owner, attr, make in targets:
             if owner is None or not hasattr(owner, attr):
                 continue

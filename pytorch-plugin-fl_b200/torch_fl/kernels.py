@@ -314,6 +314,43 @@ def softmax(x: torch.Tensor, dim: int = -1, out_dtype: torch.dtype | None = None
     return out
 
 
+def _as_bhqk(x: torch.Tensor) -> torch.Tensor:
+    if not 2 <= x.dim() <= 4:
+        raise ValueError("x must be [Q, K], [H, Q, K] or [B, H, Q, K]")
+    while x.dim() < 4:
+        x = x.unsqueeze(0)
+    return x
+
+
+def masked_softmax(x: torch.Tensor, mask: torch.Tensor | None = None, scale: float = 1.0,
+                   out_dtype: torch.dtype | None = None, rounding: str = "fused") -> torch.Tensor:
+    """softmax(x * scale + mask) over the last dim, HF eager attention's tail
+    (modeling_qwen3.py eager_attention_forward: scale, mask add,
+    softmax(dtype=float32), cast back) in one launch.  x is [B, H, Q, K] (or
+    fewer leading dims); mask has x's dtype and broadcasts to x; out_dtype
+    None = x.dtype (the cast back fused), or float32."""
+    out_dtype = out_dtype or x.dtype
+    x4 = _as_bhqk(x)
+    B, H, Q, K = x4.shape
+    x4, rows, cols, ld = _rows_or_contig(x4)
+    mp, sb, sh, sq = 0, 0, 0, 0
+    if mask is not None:
+        if mask.dtype != x.dtype:
+            raise TypeError("mask must have x's dtype")
+        m = mask.expand(x4.shape)
+        if K > 1 and m.stride(3) != 1:
+            m = m.contiguous()
+        mask = m
+        mp, sb, sh, sq = m.data_ptr(), m.stride(0), m.stride(1), m.stride(2)
+    out = torch.empty(x4.shape, dtype=out_dtype, device=x.device)
+    if out.numel():
+        with _on_device(x):
+            _abi.call("fl_b200_softmax_masked", x4.data_ptr(), ld, mp, sb, sh, sq,
+                      out.data_ptr(), cols, rows, cols, H, Q, float(scale), dtype_code(x),
+                      _DT[out_dtype], _ROUND[rounding], _stream(x))
+    return out.view(x.shape)
+
+
 # ------------------------------------------------------------------ reductions
 def _workspace(rows: int, cols: int, device) -> torch.Tensor | None:
     n = _abi.lib().fl_b200_reduce_workspace_size(rows, cols)
@@ -489,9 +526,10 @@ def silu_backward(dout: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
 
 
 def softmax_backward(dy: torch.Tensor, y: torch.Tensor,
-                     out_dtype: torch.dtype | None = None) -> torch.Tensor:
-    """dx = y * (dy - sum(dy * y)) over the last dim; out_dtype defaults to
-    y's dtype (a 16-bit dtype with fp32 dy/y: half_to_float's backward)."""
+                     out_dtype: torch.dtype | None = None, scale: float = 1.0) -> torch.Tensor:
+    """dx = scale * y * (dy - sum(dy * y)) over the last dim; out_dtype
+    defaults to y's dtype (a 16-bit dtype with fp32 dy/y: half_to_float's
+    backward).  scale != 1 is the backward of masked_softmax."""
     if dy.shape != y.shape or dy.dtype != y.dtype:
         raise ValueError("dy and y must match")
     out_dtype = out_dtype or y.dtype
@@ -501,6 +539,7 @@ def softmax_backward(dy: torch.Tensor, y: torch.Tensor,
     dy, _, _, lddy = _rows_or_contig(dy)
     dx = torch.empty(y.shape, dtype=out_dtype, device=y.device)
     with _on_device(y):
-        _abi.call("fl_b200_softmax_bwd", dy.data_ptr(), lddy, y.data_ptr(), ldy, dx.data_ptr(),
-                  cols, rows, cols, dtype_code(y), _DT[out_dtype], _stream(y))
+        _abi.call("fl_b200_softmax_bwd_scaled", dy.data_ptr(), lddy, y.data_ptr(), ldy,
+                  dx.data_ptr(), cols, rows, cols, float(scale), dtype_code(y), _DT[out_dtype],
+                  _stream(y))
     return dx

@@ -63,3 +63,15 @@ def causal_softmax(x, offset: int = 0, dtype: torch.dtype | None = None):
     applied in the kernel: query i sees keys j <= i + offset; masked entries
     are exact zeros and are never read."""
     return torch.ops.flagos.causal_softmax(x, int(offset), dtype)
+
+
+def masked_softmax(x, mask=None, scale: float = 1.0, dtype: torch.dtype | None = None,
+                   rounding: str | None = None):
+    """softmax(x * scale + mask) over the last dim in one launch: the tail of
+    HF's eager attention (modeling_qwen3.py eager_attention_forward,
+    `attn_weights * scaling + attention_mask`, softmax(dtype=float32), then
+    `.to(query.dtype)`).  x is [B, H, Q, K] (or fewer leading dims); mask has
+    x's dtype and broadcasts to x; dtype None = x's dtype (the cast back
+    fused) or float32."""
+    return torch.ops.flagos.masked_softmax(x, mask, float(scale), dtype,
+                                           rounding or default_rounding())

@@ -265,6 +265,46 @@ def main() -> None:
                   ("dk_out", dk_o), ("dq", qg.grad), ("dk", kg.grad)):
         _store(d, f"rope_bwd_f32/{k_}", t)
 
+    # HF eager attention (modeling_qwen3.eager_attention_forward) with the
+    # mask transformers itself builds (masking_utils.eager_mask: causal, and
+    # batch 1 left-padded by 5 tokens, so its first 5 queries see no key and
+    # the reference's softmax makes their rows uniform).  `w` is the bf16
+    # q @ repeat_kv(k)^T the function computes before its softmax tail.
+    import types
+
+    from transformers import masking_utils
+
+    g = _gen(14)
+    B, Hq, Hk, L, D = 2, 4, 2, 64, 32
+    scaling = D ** -0.5
+    q = torch.randn(B, Hq, L, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, Hk, L, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, Hk, L, D, generator=g).to(torch.bfloat16)
+    keep = torch.ones(B, L, dtype=torch.bool)
+    keep[1, :5] = False
+    mask = masking_utils.eager_mask(batch_size=B, q_length=L, kv_length=L, attention_mask=keep,
+                                    dtype=torch.bfloat16)
+    module = types.SimpleNamespace(num_key_value_groups=Hq // Hk, training=False)
+    attn_out, attn_w = mq.eager_attention_forward(module, q, k, v, mask, scaling)
+    w = torch.matmul(q, mq.repeat_kv(k, Hq // Hk).transpose(2, 3))
+    wg = w.clone().requires_grad_(True)
+    y = torch.softmax(wg * scaling + mask, dim=-1, dtype=torch.float32).to(torch.bfloat16)
+    assert torch.equal(y.detach(), attn_w)
+    dy = torch.randn(B, Hq, L, L, generator=g).to(torch.bfloat16)
+    y.backward(dy)
+    z32 = (w * scaling + mask).float()  # what _softmax(float32) receives op by op
+    for k_, t in (("w", w), ("mask", mask), ("attn_weights", attn_w), ("dy", dy),
+                  ("dw", wg.grad), ("z32", z32), ("z32_softmax", torch.softmax(z32, dim=-1))):
+        _store(d, f"masked_softmax_bf16/{k_}", t)
+    d["masked_softmax_bf16/scaling:f32"] = np.array([scaling], np.float32)
+    # fp32 model: the mask holds float32's lowest value
+    wf = torch.randn(B, Hq, L, L, generator=g)
+    maskf = masking_utils.eager_mask(batch_size=B, q_length=L, kv_length=L, attention_mask=keep,
+                                     dtype=torch.float32)
+    yf = torch.softmax(wf * scaling + maskf, dim=-1, dtype=torch.float32)
+    for k_, t in (("w", wf), ("mask", maskf), ("out", yf)):
+        _store(d, f"masked_softmax_f32/{k_}", t)
+
     np.savez_compressed(OUT, **d)
     print(f"wrote {OUT}: {len(d)} arrays, {os.path.getsize(OUT)} bytes")
 

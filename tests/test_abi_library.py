@@ -76,6 +76,16 @@ def test_workspace_size_plan():
     lambda: _abi.call("fl_b200_rope_qk", 8, 8, 1, 0, 0, 0, 0, 0, 0, None, None, 0, 0, 0, 0,
                       0, 0, 0, 8, 8, 0, 0, 1, 1, 3, 1, 0, None),  # odd head dim
     lambda: _abi.call("fl_b200_reduce_middim", None, 1, 1, 1, None, 5, 0, 0, None),
+    # masked softmax: rows not a whole number of (heads x q_len) blocks, no
+    # heads, an unknown rounding mode
+    lambda: _abi.call("fl_b200_softmax_masked", 16, 8, None, 0, 0, 0, 16, 8, 6, 8, 2, 4, 1.0,
+                      1, 1, 0, None),
+    lambda: _abi.call("fl_b200_softmax_masked", 16, 8, None, 0, 0, 0, 16, 8, 8, 8, 0, 4, 1.0,
+                      1, 1, 0, None),
+    lambda: _abi.call("fl_b200_softmax_masked", 16, 8, None, 0, 0, 0, 16, 8, 8, 8, 2, 4, 1.0,
+                      1, 1, 7, None),
+    lambda: _abi.call("fl_b200_softmax_bwd_scaled", None, 0, None, 0, None, 0, -1, 4, 1.0, 1, 1,
+                      None),
 ])
 def test_bad_arguments_are_rejected_on_the_host(call):
     with pytest.raises(_abi.FlB200Error) as ei:
@@ -89,3 +99,5 @@ def test_empty_inputs_are_no_ops():
     _abi.call("fl_b200_swiglu", None, 0, None, 0, None, 0, 0, 8, 1, 0, None)
     _abi.call("fl_b200_cast", None, 0, None, 1, 0, None)
     _abi.call("fl_b200_softmax_lastdim", None, 0, None, 0, 0, 4, 1, 1, 0, 1, 0, None)
+    _abi.call("fl_b200_softmax_masked", None, 0, None, 0, 0, 0, None, 0, 0, 64, 4, 16, 0.125,
+              1, 1, 0, None)

@@ -43,7 +43,7 @@ def test_qwen3_forward_on_flagos_matches_cpu():
 
 
 def test_qwen3_forward_with_fused_hooks(monkeypatch):
-    calls = {"rms_norm": 0, "rope_qk": 0, "swiglu": 0}
+    calls = {"rms_norm": 0, "rope_qk": 0, "swiglu": 0, "masked_softmax": 0}
     for name in calls:
         orig = getattr(torch_fl.ops, name)
 
@@ -62,6 +62,28 @@ def test_qwen3_forward_with_fused_hooks(monkeypatch):
         out = model_d(ids.to("flagos:0")).logits
     # 2 layers x (input + post-attention + q_norm + k_norm) + final norm
     assert calls["rms_norm"] >= 9 and calls["rope_qk"] == 2 and calls["swiglu"] == 2, calls
+    assert calls["masked_softmax"] == 2, calls     # eager attention, one per layer
+    torch.testing.assert_close(out.cpu(), ref, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("hooks", [True, False])
+def test_qwen3_left_padded_batch_matches_cpu(hooks):
+    """A left-padded batch: HF's eager mask leaves the padding queries with
+    no visible key (every logit at float32's lowest value), which the
+    reference's softmax turns into uniform rows.  With the hooks the
+    attention tail is flagos::masked_softmax; without them HF's op chain
+    runs on flagos (mask add, then _softmax on the b200 route)."""
+    model = tiny_qwen3(torch.float32)
+    ids = torch.randint(0, 512, (2, 40), generator=torch.Generator().manual_seed(4))
+    am = torch.ones(2, 40, dtype=torch.long)
+    am[1, :6] = 0
+    with torch.no_grad():
+        ref = model(ids, attention_mask=am).logits
+        model_d = model.to("flagos:0")
+        if hooks:
+            torch_fl.enable_hf_fused_ops()
+        out = model_d(ids.to("flagos:0"), attention_mask=am.to("flagos:0")).logits
+    assert torch.isfinite(out.cpu()).all()
     torch.testing.assert_close(out.cpu(), ref, rtol=1e-3, atol=1e-3)
 
 

@@ -113,3 +113,37 @@ def test_two_gloo_ranks_gather_and_max():
         g, m = out[r]
         assert g == [[[0.0] * 3] * 2, [[1.0] * 3] * 2]
         assert m == 3.0
+
+
+def test_hf_hooks_install_and_leave_cpu_tensors_alone():
+    """enable_hf_fused_ops patches RMSNorm, RoPE, the MLP and the eager
+    attention of a model file; on CPU tensors every hook runs the original
+    HF code, so a left-padded batch gives the same logits bit for bit, and
+    disable_hf_fused_ops restores the originals."""
+    import torch_fl
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    from transformers.models.qwen3 import modeling_qwen3 as mq
+
+    cfg = Qwen3Config(vocab_size=128, hidden_size=64, intermediate_size=128,
+                      num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                      head_dim=16, max_position_embeddings=64, attn_implementation="eager")
+    torch.manual_seed(0)
+    model = Qwen3ForCausalLM(cfg).eval()
+    ids = torch.randint(0, 128, (2, 12), generator=torch.Generator().manual_seed(5))
+    am = torch.ones(2, 12, dtype=torch.long)
+    am[1, :3] = 0
+    with torch.no_grad():
+        ref = model(ids, attention_mask=am).logits
+    orig = mq.eager_attention_forward
+    try:
+        patched = torch_fl.enable_hf_fused_ops(models=("qwen3",))
+        for site in ("Qwen3RMSNorm.forward", "Qwen3MLP.forward", "apply_rotary_pos_emb",
+                     "eager_attention_forward"):
+            assert any(p.endswith(site) for p in patched), (site, patched)
+        assert mq.eager_attention_forward.__wrapped__ is orig
+        with torch.no_grad():
+            out = model(ids, attention_mask=am).logits
+    finally:
+        torch_fl.disable_hf_fused_ops()
+    assert mq.eager_attention_forward is orig
+    assert torch.equal(out, ref)

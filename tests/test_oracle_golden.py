@@ -195,3 +195,48 @@ def test_rope_backward_oracle_matches_autograd(golden):
         # the adjoint is the forward rotation with -sin (cos/sin halves repeat)
         parity.assert_rel(ops.rope_golden(d, cos, -sin, "f32"), got, rtol=1e-7, atol=1e-7,
                           what=f"{name} via -sin")
+
+
+def _masked_inputs(golden):
+    s = float(golden.get("masked_softmax_bf16/scaling")[0])
+    return golden.get("masked_softmax_bf16/w"), golden.get("masked_softmax_bf16/mask"), s
+
+
+def test_masked_softmax_logits_chain_bit_exact(golden):
+    # HF eager attention: `w * scaling + mask` as two rounded bf16 ops
+    w, mask, s = _masked_inputs(golden)
+    parity.assert_exact(ops.masked_logits_chain(w, mask, s, "bf16"),
+                        golden.get("masked_softmax_bf16/z32"), "logits")
+
+
+def test_masked_softmax_oracle_matches_hf_eager_attention(golden):
+    w, mask, s = _masked_inputs(golden)
+    ref = golden.get("masked_softmax_bf16/attn_weights")
+    # the padding queries of batch 1 see no key: uniform rows, not NaN
+    np.testing.assert_array_equal(ref[1, :, :5, :], np.float32(1.0 / 64))
+    # The chain flavour is pinned to the reference.  (The fused flavour is
+    # not: the reference rounds each logit to bf16 after the scale, a 2^-9
+    # relative change of the logit that alone moves exp by about one ulp.)
+    parity.assert_ulp(ops.masked_softmax_chain(w, mask, s, "bf16", "bf16"), ref, "bf16", 1, "chain")
+    d = ops.ulp_diff(ops.masked_softmax_chain(w, mask, s, "bf16", "bf16"), ref, "bf16")
+    assert np.mean(d == 0) > 0.99
+    z = golden.get("masked_softmax_bf16/z32")
+    parity.assert_rel(ops.softmax_golden(z, "f32"), golden.get("masked_softmax_bf16/z32_softmax"),
+                      what="softmax of the masked fp32 logits")
+    wf, mf = golden.get("masked_softmax_f32/w"), golden.get("masked_softmax_f32/mask")
+    assert mf.min() == np.finfo(np.float32).min
+    parity.assert_rel(ops.masked_softmax_golden(wf, mf, s, "f32"), golden.get("masked_softmax_f32/out"),
+                      what="f32")
+
+
+def test_masked_softmax_backward_oracle_matches_autograd(golden):
+    w, mask, s = _masked_inputs(golden)
+    dy = golden.get("masked_softmax_bf16/dy")
+    y = ops.masked_softmax_chain(w, mask, s, "bf16", "f32")
+    # The reference's backward uses its own fp32 probabilities (of the
+    # bf16-rounded logits) and rounds the softmax's input gradient to bf16
+    # before the scale: one more bf16 rounding than the fused formula.
+    parity.assert_within(ops.softmax_bwd_golden(dy, y, "bf16", s), golden.get("masked_softmax_bf16/dw"),
+                         s * (4 * parity.BWD_TERM_TOL * ops.softmax_bwd_bound(dy, y)
+                              + parity.ulp_of(ops.softmax_bwd_golden(dy, y, "f32"), "bf16")),
+                         "dw", dtype="bf16")

@@ -11,6 +11,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "../../../include/fl_b200.h"
 
@@ -197,6 +198,68 @@ __device__ __forceinline__ uint4 pack<__half>(const float (&f)[8]) {
     w[i] = *reinterpret_cast<uint32_t*>(&h);
   }
   return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// ------------------------------------------------------ fp32 pairs ---------
+// sm_100 runs fma / add / mul on two fp32 values held in a 64-bit register
+// pair with one instruction (PTX .f32x2); each lane is rounded exactly like
+// the scalar instruction (.rn, no contraction across the explicit ops), so
+// results equal fmaf / __fadd_rn / __fmul_rn lane by lane.
+__device__ __forceinline__ uint64_t f2_make(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float f2_lo(uint64_t r) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+  return lo;
+}
+__device__ __forceinline__ float f2_hi(uint64_t r) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+  return hi;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// Rounds both lanes of a pair to T and back (round_to<T> on each lane), two
+// values per conversion instruction (cvt.rn.{bf16x2,f16x2}.f32).
+template <typename T>
+__device__ __forceinline__ uint64_t round_pair(uint64_t p) {
+  if constexpr (std::is_same<T, float>::value) {
+    return p;
+  } else {
+    const float lo = f2_lo(p), hi = f2_hi(p);
+    uint32_t h;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
+      return f2_make(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u));
+    } else {
+      asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
+      const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&h));
+      return f2_make(v.x, v.y);
+    }
+  }
+}
+// Max of three fp32 values in one instruction (sm_100); NaN inputs are
+// ignored unless all are NaN, as with fmaxf.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // ---------------------------------------------------------- reductions ------

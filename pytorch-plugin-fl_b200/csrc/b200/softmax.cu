@@ -447,20 +447,50 @@ __device__ __forceinline__ float masked_logit(float x, float scale, float mk) {
   }
 }
 
-// Rows in registers as fp32 logits: x and mask packs are loaded together,
-// turned into logits, max, exps in place, sum, one store pass.  The mask is
-// read through L2: the rows of one batch's heads are scheduled together, so
-// a [B, 1, Q, K] mask comes from DRAM about once per batch.
+// A pack of -inf in T's encoding.
+template <typename T>
+__device__ __forceinline__ uint4 neg_inf_pack() {
+  if constexpr (std::is_same<T, float>::value) {
+    return make_uint4(0xff800000u, 0xff800000u, 0xff800000u, 0xff800000u);
+  } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
+  } else {
+    return make_uint4(0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u, 0xfc00fc00u);
+  }
+}
+
+// Rows in registers as fp32 logits in pairs: x and mask packs are loaded
+// together, turned into logits (fma.f32x2), max (3-input max), exps in
+// place, sum and scaling in pairs, one store pass.  Lanes past the row load
+// x = 0 and mask = -inf, so their logit is -inf for any finite scale with no
+// per-element select (without a mask, in-range lanes add a zero pack).  The
+// mask is read through L2: the rows of one batch's heads are scheduled
+// together, so a [B, 1, Q, K] mask comes from DRAM about once per batch.
+//
+// Row geometry (measured on B200, HF-masked [8, 32, L, L] logits): rows of up
+// to 256 packs run one warp per row with 8 packs per thread, 2 CTAs per SM
+// (bf16 L = 2048: 6.14 TB/s); longer rows 4 packs per thread at 4 CTAs of
+// 256 threads per SM (f16 L = 4096: 5.22 TB/s against 4.89 with 8 packs at 2
+// CTAs).  Same-dtype outputs use a persistent grid: with no CTA-wide barrier
+// between a warp's rows, the warps of a resident CTA never wait for its
+// slowest row (6.14 vs 5.57 TB/s for one CTA per row group).
+template <int BLOCK, int VPT>
+constexpr int masked_min_blocks() {
+  return (BLOCK <= 256 && VPT <= 4) ? 4 : ladder_min_blocks<BLOCK>();
+}
+
 template <typename TI, typename TO, int TPR, int VPT, int BLOCK, bool MASK, bool CHAIN, bool W32>
-__global__ void __launch_bounds__(BLOCK, ladder_min_blocks<BLOCK>())
+__global__ void __launch_bounds__(BLOCK, (masked_min_blocks<BLOCK, VPT>()))
 softmax_masked_kernel(const TI* __restrict__ x, int64_t ldx, const TI* __restrict__ mask,
                       MaskRows mg, TO* __restrict__ y, int64_t ldy, int64_t rows, int nvec,
                       float scale) {
   constexpr int VW = Elem<TI>::kVec;
+  constexpr int NP = VW / 2;  // fp32 pairs per pack
   constexpr int RPB = BLOCK / TPR;
   __shared__ float smem[BLOCK / 32];
   const int slot = threadIdx.x / TPR;
   const int lane = threadIdx.x % TPR;
+  const uint64_t scale2 = f2_make(scale, scale);
   for (int64_t base = (int64_t)blockIdx.x * RPB; base < rows;
        base += (int64_t)gridDim.x * RPB) {
     const int64_t row = base + slot;
@@ -473,47 +503,61 @@ softmax_masked_kernel(const TI* __restrict__ x, int64_t ldx, const TI* __restric
       const int vi = lane + i * TPR;
       const bool in = ok && vi < nvec;
       xv[i] = in ? ld_stream(xr + (int64_t)vi * VW) : make_uint4(0, 0, 0, 0);
-      if constexpr (MASK) mv[i] = in ? ld_stream(mr + (int64_t)vi * VW) : make_uint4(0, 0, 0, 0);
+      if constexpr (MASK) mv[i] = in ? ld_stream(mr + (int64_t)vi * VW) : neg_inf_pack<TI>();
+      else mv[i] = in ? make_uint4(0, 0, 0, 0) : neg_inf_pack<TI>();
     }
-    float v[VPT][VW];
+    uint64_t v[VPT][NP];
     float m = -INFINITY;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
-      const bool in = ok && lane + i * TPR < nvec;
       float f[VW], mk[VW];
       unpack<TI>(xv[i], f);
-      if constexpr (MASK) unpack<TI>(mv[i], mk);
+      unpack<TI>(mv[i], mk);
 #pragma unroll
-      for (int e = 0; e < VW; ++e) {
-        v[i][e] = in ? masked_logit<TI, MASK, CHAIN>(f[e], scale, MASK ? mk[e] : 0.f) : -INFINITY;
-        m = fmaxf(m, v[i][e]);
+      for (int p = 0; p < NP; ++p) {
+        const uint64_t xp = f2_make(f[2 * p], f[2 * p + 1]);
+        const uint64_t mp = f2_make(mk[2 * p], mk[2 * p + 1]);
+        if constexpr (CHAIN) {  // masked_logit's chain rounding, a pair at a time
+          v[i][p] = round_pair<TI>(f2_add(round_pair<TI>(f2_mul(xp, scale2)), mp));
+        } else {
+          v[i][p] = f2_fma(xp, scale2, mp);
+        }
+        m = fmax3(m, f2_lo(v[i][p]), f2_hi(v[i][p]));
       }
     }
     m = row_reduce<FastMaxOp, TPR, BLOCK>(m, smem);
     if (wide_max(m)) {
+      const uint64_t nm = f2_make(-m, -m);
 #pragma unroll
       for (int i = 0; i < VPT; ++i)
 #pragma unroll
-        for (int e = 0; e < VW; ++e) v[i][e] -= m;
+        for (int p = 0; p < NP; ++p) v[i][p] = f2_add(v[i][p], nm);
       m = 0.f;
     }
     const float ml = m * kLog2e;
-    float s = 0.f;
+    const uint64_t log2e2 = f2_make(kLog2e, kLog2e), nml2 = f2_make(-ml, -ml);
+    uint64_t acc = f2_make(0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
 #pragma unroll
-      for (int e = 0; e < VW; ++e) v[i][e] = exp_shifted(v[i][e], ml);
-      float t[VW];
+      for (int p = 0; p < NP; ++p) {
+        const uint64_t t = f2_fma(v[i][p], log2e2, nml2);
+        v[i][p] = f2_make(ex2_approx(f2_lo(t)), ex2_approx(f2_hi(t)));
+      }
+      // the pack's pairs as a tree, then into the running pair sum
+      uint64_t t[NP];
 #pragma unroll
-      for (int e = 0; e < VW; ++e) t[e] = v[i][e];
+      for (int p = 0; p < NP; ++p) t[p] = v[i][p];
 #pragma unroll
-      for (int w = VW / 2; w >= 1; w /= 2)
+      for (int w = NP / 2; w >= 1; w /= 2)
 #pragma unroll
-        for (int e = 0; e < w; ++e) t[e] += t[e + w];
-      s += t[0];
+        for (int p = 0; p < w; ++p) t[p] = f2_add(t[p], t[p + w]);
+      acc = f2_add(acc, t[0]);
     }
+    float s = f2_lo(acc) + f2_hi(acc);
     s = row_reduce<SumOp, TPR, BLOCK>(s, smem);
     const float inv = 1.0f / s;
+    const uint64_t inv2 = f2_make(inv, inv);
     TO* yr = y + row * ldy;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -521,7 +565,11 @@ softmax_masked_kernel(const TI* __restrict__ x, int64_t ldx, const TI* __restric
       if (!ok || vi >= nvec) continue;
       float o[VW];
 #pragma unroll
-      for (int e = 0; e < VW; ++e) o[e] = v[i][e] * inv;
+      for (int p = 0; p < NP; ++p) {
+        const uint64_t t = f2_mul(v[i][p], inv2);
+        o[2 * p] = f2_lo(t);
+        o[2 * p + 1] = f2_hi(t);
+      }
       store_vals<TO, VW, W32>(yr + (int64_t)vi * VW, o);
     }
   }
@@ -571,23 +619,48 @@ int launch_softmax_masked(const TI* x, int64_t ldx, const TI* mask, const MaskRo
   const bool vec_ok = mask_ok && aligned16(x) && aligned16(y) && cols % VW == 0 &&
                       ldx % VW == 0 && ldy % VW == 0;
   if (vec_ok) {
-    const int r = row_ladder<8>(cols / VW, [&](auto tpr, auto vpt) -> int {
+    const int64_t nvec = cols / VW;
+    auto go = [&](auto tpr, auto vpt) -> int {
       constexpr int TPR = decltype(tpr)::value;
       constexpr int VPT = decltype(vpt)::value;
       constexpr int BLOCK = ladder_block<TPR>();
-      const int grid = full_grid(ceil_div(rows, BLOCK / TPR));
+      const int64_t groups = ceil_div(rows, BLOCK / TPR);
       if constexpr (std::is_same<TO, float>::value && VW == 8) {
+        // fp32 outputs of 16-bit logits: one CTA per row group (bf16 L = 2048:
+        // 5.28 vs 4.86 TB/s persistent; the wider stores keep more in flight)
+        const int grid = full_grid(groups);
         if (aligned32(y) && ldy % 8 == 0) {
           softmax_masked_kernel<TI, TO, TPR, VPT, BLOCK, MASK, CHAIN, true>
-              <<<grid, BLOCK, 0, stream>>>(x, ldx, mask, mg, y, ldy, rows, (int)(cols / VW),
-                                           scale);
-          return launch_status();
+              <<<grid, BLOCK, 0, stream>>>(x, ldx, mask, mg, y, ldy, rows, (int)nvec, scale);
+        } else {
+          softmax_masked_kernel<TI, TO, TPR, VPT, BLOCK, MASK, CHAIN, false>
+              <<<grid, BLOCK, 0, stream>>>(x, ldx, mask, mg, y, ldy, rows, (int)nvec, scale);
         }
+        return launch_status();
+      } else {
+        // resident CTAs per SM of this instantiation
+        static const int per_sm = blocks_per_sm(
+            softmax_masked_kernel<TI, TO, TPR, VPT, BLOCK, MASK, CHAIN, false>, BLOCK, 0);
+        const int grid = (int)std::max<int64_t>(
+            1, std::min<int64_t>(groups, (int64_t)per_sm * dev.sm_count));
+        softmax_masked_kernel<TI, TO, TPR, VPT, BLOCK, MASK, CHAIN, false>
+            <<<grid, BLOCK, 0, stream>>>(x, ldx, mask, mg, y, ldy, rows, (int)nvec, scale);
+        return launch_status();
       }
-      softmax_masked_kernel<TI, TO, TPR, VPT, BLOCK, MASK, CHAIN, false>
-          <<<grid, BLOCK, 0, stream>>>(x, ldx, mask, mg, y, ldy, rows, (int)(cols / VW), scale);
-      return launch_status();
-    });
+    };
+    int r = -1;
+    if constexpr (std::is_same<TO, float>::value && VW == 8) {
+      r = row_ladder<8>(nvec, go);
+    } else if (nvec <= 256) {
+      r = row_ladder<8>(nvec, go);
+    } else {  // 4 packs per thread, 4 CTAs of 256 threads per SM
+      using std::integral_constant;
+      using V4 = integral_constant<int, 4>;
+      if (nvec <= 512) r = go(integral_constant<int, 128>{}, V4{});
+      else if (nvec <= 1024) r = go(integral_constant<int, 256>{}, V4{});
+      else if (nvec <= 2048) r = go(integral_constant<int, 512>{}, V4{});
+      else if (nvec <= 4096) r = go(integral_constant<int, 1024>{}, V4{});
+    }
     if (r >= 0) return r;
   }
   auto kern = softmax_masked_loop_kernel<TI, TO, MASK, CHAIN>;

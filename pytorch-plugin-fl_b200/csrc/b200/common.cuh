@@ -235,23 +235,37 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+// A pair as the 32-bit word of two 16-bit T values (round to nearest even,
+// one cvt.rn.{bf16x2,f16x2}.f32; lo in the low half, as in memory) and back.
+template <typename T>
+__device__ __forceinline__ uint32_t pair_to_bits(uint64_t p) {
+  static_assert(!std::is_same<T, float>::value, "16-bit types only");
+  const float lo = f2_lo(p), hi = f2_hi(p);
+  uint32_t h;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
+  } else {
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
+  }
+  return h;
+}
+template <typename T>
+__device__ __forceinline__ uint64_t pair_from_bits(uint32_t h) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return f2_make(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u));
+  } else {
+    const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&h));
+    return f2_make(v.x, v.y);
+  }
+}
 // Rounds both lanes of a pair to T and back (round_to<T> on each lane), two
-// values per conversion instruction (cvt.rn.{bf16x2,f16x2}.f32).
+// values per conversion instruction.
 template <typename T>
 __device__ __forceinline__ uint64_t round_pair(uint64_t p) {
   if constexpr (std::is_same<T, float>::value) {
     return p;
   } else {
-    const float lo = f2_lo(p), hi = f2_hi(p);
-    uint32_t h;
-    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
-      return f2_make(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u));
-    } else {
-      asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
-      const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&h));
-      return f2_make(v.x, v.y);
-    }
+    return pair_from_bits<T>(pair_to_bits<T>(p));
   }
 }
 // Max of three fp32 values in one instruction (sm_100); NaN inputs are

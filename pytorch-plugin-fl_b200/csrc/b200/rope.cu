@@ -152,6 +152,19 @@ __global__ void __launch_bounds__(256) rope_token_kernel(RopeArgs a, uint32_t to
     unpack<T>(ld_cached(cb + half + dl), ch);
     unpack<T>(ld_cached(sb + dl), sl);
     unpack<T>(ld_cached(sb + half + dl), sh);
+    // fused rounding: the rotation in fp32 pairs, sin of the low half negated
+    // once per token (x*(-s) is exactly -(x*s), so the results equal the
+    // scalar fmaf(xl, cl, -xh*sl), fmaf(xh, ch, xl*sh) bit for bit)
+    uint64_t cl2[VW / 2], ch2[VW / 2], nsl2[VW / 2], sh2[VW / 2];
+    if constexpr (!CHAIN) {
+#pragma unroll
+      for (int p = 0; p < VW / 2; ++p) {
+        cl2[p] = f2_make(cl[2 * p], cl[2 * p + 1]);
+        ch2[p] = f2_make(ch[2 * p], ch[2 * p + 1]);
+        nsl2[p] = f2_make(-sl[2 * p], -sl[2 * p + 1]);
+        sh2[p] = f2_make(sh[2 * p], sh[2 * p + 1]);
+      }
+    }
     for (uint32_t h0 = 0; h0 < htot; h0 += SLOTS * U) {  // warp-uniform
       uint4 lo[U], hi[U];
       T* dst[U];
@@ -209,9 +222,23 @@ __global__ void __launch_bounds__(256) rope_token_kernel(RopeArgs a, uint32_t to
         }
         if (!valid[u]) continue;
         float ol[VW], oh[VW];
+        if constexpr (CHAIN) {
 #pragma unroll
-        for (int e = 0; e < VW; ++e)
-          rope_pair<T, CHAIN>(xl[e], xh[e], cl[e], sl[e], ch[e], sh[e], ol[e], oh[e]);
+          for (int e = 0; e < VW; ++e)
+            rope_pair<T, CHAIN>(xl[e], xh[e], cl[e], sl[e], ch[e], sh[e], ol[e], oh[e]);
+        } else {
+#pragma unroll
+          for (int p = 0; p < VW / 2; ++p) {
+            const uint64_t xl2 = f2_make(xl[2 * p], xl[2 * p + 1]);
+            const uint64_t xh2 = f2_make(xh[2 * p], xh[2 * p + 1]);
+            const uint64_t o1 = f2_fma(xl2, cl2[p], f2_mul(xh2, nsl2[p]));
+            const uint64_t o2 = f2_fma(xh2, ch2[p], f2_mul(xl2, sh2[p]));
+            ol[2 * p] = f2_lo(o1);
+            ol[2 * p + 1] = f2_hi(o1);
+            oh[2 * p] = f2_lo(o2);
+            oh[2 * p + 1] = f2_hi(o2);
+          }
+        }
         st_stream(dst[u] + dl, pack<T>(ol));
         st_stream(dst[u] + half + dl, pack<T>(oh));
       }

@@ -31,11 +31,25 @@ namespace {
 // fixed, so dw does not depend on timing.  The next row's x and dy are
 // loaded while the current row is reduced and stored (two row buffers in
 // registers, 3 CTAs per SM): measured on B200, bf16 [65536, 4096] 5.73 vs
-// 5.44 TB/s with one buffer at 4 CTAs per SM.
+// 5.44 TB/s with one buffer at 4 CTAs per SM.  Rows of 257..512 packs run
+// 128 threads x 4 packs (two rows per CTA) at 2 CTAs per SM: 6.12 vs 5.92
+// TB/s for 256 x 2 at 3 CTAs (bf16 4096-wide rows, kernel alone).
 constexpr int kBwdCtasPerSm = 3;
 
+template <int BLOCK, int VPT>
+constexpr int rms_bwd_min_blocks() {
+  return BLOCK <= 256 ? (VPT >= 4 ? 2 : kBwdCtasPerSm) : 1;
+}
+// A CTA writes one dw partial row per row slot (one-slot CTAs, and the two
+// slots of the 2-CTA rung: at most 4 partial rows per SM), else one row with
+// its slots added in slot order.
+template <int RPB, int VPT>
+__host__ __device__ constexpr bool rms_bwd_slot_rows() {
+  return RPB == 1 || (RPB == 2 && VPT >= 4);
+}
+
 template <typename T, int TPR, int VPT, int BLOCK>
-__global__ void __launch_bounds__(BLOCK, (BLOCK <= 256 ? kBwdCtasPerSm : 1))
+__global__ void __launch_bounds__(BLOCK, (rms_bwd_min_blocks<BLOCK, VPT>()))
 rms_norm_bwd_kernel(const T* __restrict__ dy, int64_t lddy, const T* __restrict__ x,
                     int64_t ldx, const T* __restrict__ w, T* __restrict__ dx, int64_t lddx,
                     float* __restrict__ partial, int64_t rows, int nvec, float eps,
@@ -109,8 +123,9 @@ rms_norm_bwd_kernel(const T* __restrict__ dy, int64_t lddy, const T* __restrict_
     }
   }
   if (partial == nullptr) return;
-  float* out = partial + (int64_t)blockIdx.x * nvec * VW;
-  if constexpr (RPB == 1) {
+  if constexpr (rms_bwd_slot_rows<RPB, VPT>()) {
+    // one partial row per row slot, in (CTA, slot) order
+    float* out = partial + ((int64_t)blockIdx.x * RPB + slot) * nvec * VW;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = lane + i * TPR;
@@ -119,6 +134,8 @@ rms_norm_bwd_kernel(const T* __restrict__ dy, int64_t lddy, const T* __restrict_
         for (int e = 0; e < VW; ++e) out[(int64_t)vi * VW + e] = acc[i][e];
     }
   } else {
+    // the CTA's row slots added in slot order into one partial row
+    float* out = partial + (int64_t)blockIdx.x * nvec * VW;
     __shared__ float part[BLOCK * VPT * VW];
 #pragma unroll
     for (int i = 0; i < VPT; ++i)
@@ -199,33 +216,41 @@ rms_norm_dw_reduce_kernel(const float* __restrict__ partial, int64_t P, int64_t 
 }
 
 // Rows of partials the backward uses on this device (an upper bound: the
-// workspace is sized from it, a launch may use fewer).
-int64_t rms_bwd_max_ctas(const DeviceInfo& dev) { return (int64_t)dev.sm_count * kBwdCtasPerSm; }
+// workspace is sized from it, a launch may use fewer): 3 CTAs of one row
+// slot, or 2 CTAs of two slots, per SM.
+int64_t rms_bwd_max_partials(const DeviceInfo& dev) { return (int64_t)dev.sm_count * 4; }
 
 template <typename T>
 int launch_rms_norm_bwd(const T* dy, int64_t lddy, const T* x, int64_t ldx, const T* w,
                         T* dx, int64_t lddx, T* dw, int64_t rows, int64_t cols, float eps,
                         float* partial, const DeviceInfo& dev, cudaStream_t stream) {
   constexpr int VW = Elem<T>::kVec;
-  const int64_t max_ctas = rms_bwd_max_ctas(dev);
-  int64_t used = 0;
+  int64_t used = 0;  // partial rows written
   const bool vec_ok = aligned16(dy) && aligned16(x) && aligned16(w) && aligned16(dx) &&
                       cols % VW == 0 && lddy % VW == 0 && ldx % VW == 0 && lddx % VW == 0;
   int st = -1;
   if (vec_ok) {
-    st = row_ladder<2>(cols / VW, [&](auto tpr, auto vpt) -> int {
+    auto go = [&](auto tpr, auto vpt) -> int {
       constexpr int TPR = decltype(tpr)::value;
       constexpr int VPT = decltype(vpt)::value;
       constexpr int BLOCK = ladder_block<TPR>();
-      const int64_t groups = ceil_div(rows, BLOCK / TPR);
-      used = std::min<int64_t>(groups, max_ctas);
-      rms_norm_bwd_kernel<T, TPR, VPT, BLOCK><<<(int)used, BLOCK, 0, stream>>>(
+      constexpr int RPB = BLOCK / TPR;
+      const int64_t groups = ceil_div(rows, RPB);
+      const int64_t ctas =
+          std::min<int64_t>(groups, (int64_t)dev.sm_count * rms_bwd_min_blocks<BLOCK, VPT>());
+      used = ctas * (rms_bwd_slot_rows<RPB, VPT>() ? RPB : 1);
+      rms_norm_bwd_kernel<T, TPR, VPT, BLOCK><<<(int)ctas, BLOCK, 0, stream>>>(
           dy, lddy, x, ldx, w, dx, lddx, partial, rows, (int)(cols / VW), eps, (float)cols);
       return launch_status();
-    });
+    };
+    const int64_t nvec = cols / VW;
+    if (nvec > 256 && nvec <= 512)
+      st = go(std::integral_constant<int, 128>{}, std::integral_constant<int, 4>{});
+    else
+      st = row_ladder<2>(nvec, go);
   }
   if (st < 0) {
-    used = std::min<int64_t>(rows, max_ctas);
+    used = std::min<int64_t>(rows, (int64_t)dev.sm_count * kBwdCtasPerSm);
     rms_norm_bwd_loop_kernel<T><<<(int)used, 256, 0, stream>>>(dy, lddy, x, ldx, w, dx, lddx,
                                                               partial, rows, cols, eps);
     st = launch_status();
@@ -446,7 +471,7 @@ FL_B200_API size_t fl_b200_rms_norm_bwd_workspace_size(int64_t rows, int64_t col
   if (rows <= 0 || cols <= 0) return 0;
   DeviceInfo dev;
   if (current_device_info(&dev) != FL_B200_OK) return 0;
-  return (size_t)rms_bwd_max_ctas(dev) * (size_t)cols * sizeof(float);
+  return (size_t)rms_bwd_max_partials(dev) * (size_t)cols * sizeof(float);
 }
 
 FL_B200_API int fl_b200_rms_norm_bwd(const void* dy, int64_t ld_dy, const void* x,
@@ -471,7 +496,7 @@ FL_B200_API int fl_b200_rms_norm_bwd(const void* dy, int64_t ld_dy, const void* 
   if (st != FL_B200_OK) return st;
   float* partial = nullptr;
   if (dw != nullptr) {
-    const size_t need = (size_t)rms_bwd_max_ctas(dev) * (size_t)cols * sizeof(float);
+    const size_t need = (size_t)rms_bwd_max_partials(dev) * (size_t)cols * sizeof(float);
     if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
       return FL_B200_ERR_WORKSPACE;
     partial = static_cast<float*>(workspace);

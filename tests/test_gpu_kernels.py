@@ -87,16 +87,51 @@ def test_rms_norm_strided_and_inplace():
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-def test_add_rms_norm(dtype):
-    x = rnd((48, 4096), dtype, 8)
-    y = rnd((48, 4096), dtype, 9)
-    w = rnd((4096,), dtype, 10, scale=0.1, loc=1.0)
-    out, h = K.add_rms_norm(x, y, w, 1e-5)
+@pytest.mark.parametrize("cols", [4096, 8192, 16384, 1024, 2048, 4104, 40])
+def test_add_rms_norm(dtype, cols):
+    # 32-byte path: one pack per thread (4096, 8192, 16384 16-bit wide), the
+    # two-pack ladder (1024, 2048; fp32 40); 4104 and 40 16-bit values are
+    # not whole 32-byte packs: the 16-byte kernel
+    x = rnd((48, cols), dtype, 8)
+    y = rnd((48, cols), dtype, 9)
+    w = rnd((cols,), dtype, 10, scale=0.1, loc=1.0)
     dt = parity.dname(dtype)
-    ref_o, ref_h = ops.add_rms_norm_golden(parity.to_np(x), parity.to_np(y), parity.to_np(w), 1e-5, dt)
+    xn, yn, wn = parity.to_np(x), parity.to_np(y), parity.to_np(w)
+    out, h = K.add_rms_norm(x, y, w, 1e-5)
+    ref_o, ref_h = ops.add_rms_norm_golden(xn, yn, wn, 1e-5, dt)
     check_float(h, ref_h, dt, "h")
     # the norm is taken over the stored (rounded) h
-    check_float(out, ops.rms_norm_golden(parity.to_np(h), parity.to_np(w), 1e-5, dt), dt, "out")
+    check_float(out, ops.rms_norm_golden(parity.to_np(h), wn, 1e-5, dt), dt, "out")
+    # chain rounding: h exact, the norm rounded where the reference's chain
+    # rounds (16-bit: differs only where the fp32 sum order flips the
+    # intermediate rounding of h*r, as for RMSNorm alone; fp32 has no
+    # intermediate rounding, so the fused bound holds)
+    out_c, h_c = K.add_rms_norm(x, y, w, 1e-5, rounding="chain")
+    ref_oc, ref_hc = ops.add_rms_norm_chain(xn, yn, wn, 1e-5, dt)
+    check_float(h_c, ref_hc, dt, "h chain")
+    if dt == "f32":
+        check_float(out_c, ref_oc, dt, "out chain")
+    else:
+        d = parity.assert_ulp(parity.to_np(out_c), ref_oc, dt, 2, "out chain")
+        assert np.mean(d == 0) > 0.99
+
+
+def test_add_rms_norm_unaligned_rows_take_the_other_paths():
+    # a base offset of one element (16-byte but not 32-byte aligned rows
+    # would need 8-element offsets): the looped kernel; 8 elements: the
+    # 16-byte kernel; both must give the 32-byte kernel's values
+    base_x = rnd((16, 4096 + 8), torch.bfloat16, 11)
+    base_y = rnd((16, 4096 + 8), torch.bfloat16, 12)
+    w = rnd((4096,), torch.bfloat16, 13, scale=0.1, loc=1.0)
+    ref_o, ref_h = K.add_rms_norm(base_x[:, :4096].contiguous(), base_y[:, :4096].contiguous(), w,
+                                  1e-5)
+    for off in (8, 1):
+        xs = base_x.flatten()[off:off + 16 * 4096].view(16, 4096)
+        ys = base_y.flatten()[off:off + 16 * 4096].view(16, 4096)
+        o, h = K.add_rms_norm(xs, ys, w, 1e-5)
+        ro, rh = K.add_rms_norm(xs.contiguous() * 1, ys.contiguous() * 1, w, 1e-5)
+        parity.assert_ulp(parity.to_np(h), parity.to_np(rh), "bf16", 0, f"h offset {off}")
+        parity.assert_ulp(parity.to_np(o), parity.to_np(ro), "bf16", 1, f"out offset {off}")
 
 
 # ---------------------------------------------------------------------- RoPE

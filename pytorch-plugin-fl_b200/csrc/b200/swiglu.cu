@@ -109,32 +109,49 @@ swiglu_residual_kernel(const T* g, const T* u, T* act, int64_t n_act, const T* x
   add_dense<T>(x, y, h, n_res, tid, nth);
 }
 
-// 32-byte packs (two 16-byte halves per access), one per thread: the path
-// for 32-byte aligned dense tensors.  The CTAs of the grid's first
-// `act_blocks` do SwiGLU packs, the rest residual-add packs (n_res may be 0).
+// 32-byte packs (two 16-byte halves per access), two per thread (packs i
+// and i + 512 of the CTA's 1024), 512-thread CTAs: the path for 32-byte
+// aligned dense tensors.  Measured on B200, bf16 131072 x 14336 alone: 7.20
+// TB/s against 7.04 with one pack per thread in 256-thread CTAs.  The CTAs
+// of the grid's first `act_blocks` do SwiGLU packs, the rest residual-add
+// packs (n_res may be 0).
+constexpr int kBlock32 = 512;
+constexpr int kPacks32 = 2;
+
 template <typename T, bool CHAIN>
-__global__ void __launch_bounds__(kBlock)
+__global__ void __launch_bounds__(kBlock32)
 swiglu32_kernel(const T* g, const T* u, T* act, int64_t n_act, int64_t act_blocks,
                 const T* x, const T* y, T* h, int64_t n_res) {
   constexpr int VW2 = 2 * Elem<T>::kVec;  // elements per 32-byte pack
-  if ((int64_t)blockIdx.x < act_blocks) {
-    const int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x;
-    if (i < n_act) {
-      const Pack32 gv = ld_stream32(g + i * VW2), uv = ld_stream32(u + i * VW2);
-      Pack32 o;
-      o.lo = swiglu_pack<T, CHAIN>(gv.lo, uv.lo);
-      o.hi = swiglu_pack<T, CHAIN>(gv.hi, uv.hi);
-      st_stream32(act + i * VW2, o);
+  const bool is_act = (int64_t)blockIdx.x < act_blocks;
+  const int64_t blk = is_act ? (int64_t)blockIdx.x : (int64_t)blockIdx.x - act_blocks;
+  const int64_t i0 = blk * (kBlock32 * kPacks32) + threadIdx.x;
+  const T* a = is_act ? g : x;
+  const T* b = is_act ? u : y;
+  T* o = is_act ? act : h;
+  const int64_t n = is_act ? n_act : n_res;
+  Pack32 av[kPacks32], bv[kPacks32];
+#pragma unroll
+  for (int k = 0; k < kPacks32; ++k) {
+    const int64_t i = i0 + (int64_t)k * kBlock32;
+    if (i < n) {
+      av[k] = ld_stream32(a + i * VW2);
+      bv[k] = ld_stream32(b + i * VW2);
     }
-  } else {
-    const int64_t i = ((int64_t)blockIdx.x - act_blocks) * kBlock + threadIdx.x;
-    if (i < n_res) {
-      const Pack32 xv = ld_stream32(x + i * VW2), yv = ld_stream32(y + i * VW2);
-      Pack32 o;
-      o.lo = add_pack<T>(xv.lo, yv.lo);
-      o.hi = add_pack<T>(xv.hi, yv.hi);
-      st_stream32(h + i * VW2, o);
+  }
+#pragma unroll
+  for (int k = 0; k < kPacks32; ++k) {
+    const int64_t i = i0 + (int64_t)k * kBlock32;
+    if (i >= n) continue;
+    Pack32 r;
+    if (is_act) {
+      r.lo = swiglu_pack<T, CHAIN>(av[k].lo, bv[k].lo);
+      r.hi = swiglu_pack<T, CHAIN>(av[k].hi, bv[k].hi);
+    } else {
+      r.lo = add_pack<T>(av[k].lo, bv[k].lo);
+      r.hi = add_pack<T>(av[k].hi, bv[k].hi);
     }
+    st_stream32(o + i * VW2, r);
   }
 }
 
@@ -143,9 +160,10 @@ int launch_swiglu32(const T* g, const T* u, T* act, int64_t n_act, const T* x, c
                     T* h, int64_t n_res, cudaStream_t stream) {
   constexpr int VW2 = 2 * Elem<T>::kVec;
   const int64_t pa = n_act / VW2, pr = n_res / VW2;
-  const int64_t ba = ceil_div(pa, kBlock), br = ceil_div(pr, kBlock);
+  constexpr int64_t kChunk = (int64_t)kBlock32 * kPacks32;
+  const int64_t ba = ceil_div(pa, kChunk), br = ceil_div(pr, kChunk);
   if (ba + br > 0x7fffffff) return FL_B200_ERR_TOO_LARGE;
-  swiglu32_kernel<T, CHAIN><<<(int)std::max<int64_t>(ba + br, 1), kBlock, 0, stream>>>(
+  swiglu32_kernel<T, CHAIN><<<(int)std::max<int64_t>(ba + br, 1), kBlock32, 0, stream>>>(
       g, u, act, pa, ba, x, y, h, pr);
   return launch_status();
 }

@@ -767,6 +767,20 @@ def op_configs(dev, peak, reps=5):
             lg * sc + hf, -1, dtype=torch.float32).to(dt), 4 * n + hf.numel() * 2,
             "the same tail as 4 PyTorch CUDA ops (bytes: the fused op's)")
         del lg, hf
+    # broadcast add / mul on the stack's activation shape: the residual add,
+    # a [hidden] weight broadcast over the rows, a [T, 1] per-row scale
+    TA = 131072
+    xa = torch.randn(TA, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+    ya = torch.randn(TA, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+    wv = torch.randn(HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+    cv = torch.randn(TA, 1, generator=g, device=dev).to(torch.bfloat16)
+    n = xa.numel()
+    timed(f"add_bf16_{TA}x{HIDDEN}", lambda: K.add(xa, ya), 3 * n * BF16)
+    timed(f"mul_bf16_{TA}x{HIDDEN}_by_row_vector", lambda: K.mul(xa, wv), 2 * n * BF16,
+          "[hidden] weight broadcast over the rows")
+    timed(f"mul_bf16_{TA}x{HIDDEN}_by_column", lambda: K.mul(xa, cv), 2 * n * BF16,
+          "[T, 1] per-row scale")
+    del xa, ya, wv, cv
     # config 4: reductions
     xf = torch.randn(65536, 8192, generator=g, device=dev)
     n = xf.numel()

@@ -211,13 +211,13 @@ __device__ __forceinline__ uint64_t f2_make(float lo, float hi) {
   return r;
 }
 __device__ __forceinline__ float f2_lo(uint64_t r) {
-  float lo, hi;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+  float lo;
+  asm("{ .reg .f32 t; mov.b64 {%0, t}, %1; }" : "=f"(lo) : "l"(r));
   return lo;
 }
 __device__ __forceinline__ float f2_hi(uint64_t r) {
-  float lo, hi;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+  float hi;
+  asm("{ .reg .f32 t; mov.b64 {t, %0}, %1; }" : "=f"(hi) : "l"(r));
   return hi;
 }
 __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {

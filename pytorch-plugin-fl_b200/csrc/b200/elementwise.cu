@@ -5,9 +5,10 @@
 // kernels with fp32 opmath for 16-bit floats; wrapped CPU scalars stay in
 // opmath (add.cu:67-76); flagos->flagos dtype casts (copy_ops.cc:225-240).
 //
-// Paths, fastest first: dense same-shape operands (16-byte packs); one
-// operand a row vector broadcast over the rows of the other (the RMSNorm
-// weight multiply, bias adds); anything else through N-d index arithmetic.
+// Paths, fastest first: dense same-shape operands (32-byte, else 16-byte
+// packs); one operand a row vector broadcast over the rows of the other
+// (the RMSNorm weight multiply, bias adds) or one value per row ([T, 1]
+// scales); anything else through N-d index arithmetic.
 #include "common.cuh"
 
 #include <algorithm>
@@ -68,22 +69,93 @@ binary_dense_kernel(const T* a, const T* b, T* o, int64_t npk, float alpha) {
   }
 }
 
-// ---- row-vector broadcast: full[r, c] op vec[c] ----------------------------
-// VEC_IS_A: the broadcast operand is `a` (vec op full), else `b`.
-template <typename T, int OP, bool VEC_IS_A>
-__global__ void __launch_bounds__(kBlock)
-binary_rowvec_kernel(const T* full, const T* vec, T* o, int64_t npk, int64_t cpk,
-                     float alpha) {
+// ---- dense same-shape, 32-byte packs ---------------------------------------
+// Two 32-byte packs per thread (packs i and i + 512 of the CTA's 1024),
+// 512-thread CTAs, one CTA per 1024 packs: for 32-byte aligned operands.
+// Measured on B200, bf16 [131072, 4096] + [131072, 4096]: 7.0 TB/s against
+// 6.3 with one 16-byte pack per thread (PyTorch's own add: 7.1).
+constexpr int kBlock32 = 512;
+constexpr int kPacks32 = 2;
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(kBlock32)
+binary_dense32_kernel(const T* a, const T* b, T* o, int64_t npk32, float alpha) {
   constexpr int VW = Elem<T>::kVec;
-  const int64_t nth = (int64_t)gridDim.x * kBlock;
-  for (int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x; i < npk; i += nth) {
-    float x[VW], v[VW];
-    unpack<T>(ld_stream(full + i * VW), x);
-    unpack<T>(ld_cached(vec + (i % cpk) * VW), v);
+  const int64_t i0 = (int64_t)blockIdx.x * (kBlock32 * kPacks32) + threadIdx.x;
+  Pack32 av[kPacks32], bv[kPacks32];
 #pragma unroll
-    for (int e = 0; e < VW; ++e)
-      x[e] = VEC_IS_A ? apply_f<OP>(v[e], x[e], alpha) : apply_f<OP>(x[e], v[e], alpha);
-    st_stream(o + i * VW, pack<T>(x));
+  for (int k = 0; k < kPacks32; ++k) {
+    const int64_t i = i0 + (int64_t)k * kBlock32;
+    if (i < npk32) {
+      av[k] = ld_stream32(a + i * 2 * VW);
+      bv[k] = ld_stream32(b + i * 2 * VW);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kPacks32; ++k) {
+    const int64_t i = i0 + (int64_t)k * kBlock32;
+    if (i >= npk32) continue;
+    float x[VW], y[VW];
+    Pack32 r;
+    unpack<T>(av[k].lo, x);
+    unpack<T>(bv[k].lo, y);
+#pragma unroll
+    for (int e = 0; e < VW; ++e) x[e] = apply_f<OP>(x[e], y[e], alpha);
+    r.lo = pack<T>(x);
+    unpack<T>(av[k].hi, x);
+    unpack<T>(bv[k].hi, y);
+#pragma unroll
+    for (int e = 0; e < VW; ++e) x[e] = apply_f<OP>(x[e], y[e], alpha);
+    r.hi = pack<T>(x);
+    st_stream32(o + i * 2 * VW, r);
+  }
+}
+
+// ---- one operand broadcast over the rows of the other -----------------------
+// full is a dense [rows, cols] operand; the other is a row vector v[c]
+// (MODE kRowVec) or one value per row s[r] at s + r * s_stride (MODE
+// kColVec).  A CTA takes kTileRows rows; each thread walks its column packs
+// (c = threadIdx.x, + kBlock, ...), loads the vector pack once per column or
+// the rows' values once (the same addresses for the whole CTA), and streams
+// the rows' packs with kTileRows loads in flight.  VEC_FIRST: the broadcast
+// operand is `a` (v op full), else `b` (full op v): the order matters for
+// add's alpha.  Measured on B200, bf16 [131072, 4096] times a [4096] row
+// vector: 6.6 TB/s (5.7 with a per-pack index modulo), times a [131072, 1]
+// column: 6.6 TB/s (0.7 through the N-d path; PyTorch: 1.8 for both).
+constexpr int kTileRows = 8;
+enum { kRowVec = 0, kColVec = 1 };
+
+template <typename T, int OP, int MODE, bool VEC_FIRST>
+__global__ void __launch_bounds__(kBlock)
+binary_bcast_rows_kernel(const T* full, const T* vec, int64_t s_stride, T* o, int64_t rows,
+                         int64_t cpk, float alpha) {
+  constexpr int VW = Elem<T>::kVec;
+  const int64_t r0 = (int64_t)blockIdx.x * kTileRows;
+  float sv[kTileRows];
+  if constexpr (MODE == kColVec) {
+#pragma unroll
+    for (int k = 0; k < kTileRows; ++k)
+      sv[k] = r0 + k < rows ? Elem<T>::to_f(vec[(r0 + k) * s_stride]) : 0.f;
+  }
+  for (int64_t c = threadIdx.x; c < cpk; c += kBlock) {
+    float v[VW];
+    if constexpr (MODE == kRowVec) unpack<T>(ld_cached(vec + c * VW), v);
+    uint4 fv[kTileRows];
+#pragma unroll
+    for (int k = 0; k < kTileRows; ++k)
+      fv[k] = r0 + k < rows ? ld_stream(full + ((r0 + k) * cpk + c) * VW) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int k = 0; k < kTileRows; ++k) {
+      if (r0 + k >= rows) continue;
+      float x[VW];
+      unpack<T>(fv[k], x);
+#pragma unroll
+      for (int e = 0; e < VW; ++e) {
+        const float w = MODE == kRowVec ? v[e] : sv[k];
+        x[e] = VEC_FIRST ? apply_f<OP>(w, x[e], alpha) : apply_f<OP>(x[e], w, alpha);
+      }
+      st_stream(o + ((r0 + k) * cpk + c) * VW, pack<T>(x));
+    }
   }
 }
 
@@ -271,6 +343,27 @@ bool rowvec_strides(const int64_t* sizes, const int64_t* st, int ndim) {
   return true;
 }
 
+// True if `st` addresses one value per row (stride 0 on the last dim) whose
+// leading dims collapse to a single row stride, returned in *row_stride:
+// e.g. a [T, 1] or [B, S, 1] tensor broadcast over the last dim.
+bool colvec_strides(const int64_t* sizes, const int64_t* st, int ndim, int64_t* row_stride) {
+  if (ndim < 2) return false;
+  if (sizes[ndim - 1] != 1 && st[ndim - 1] != 0) return false;
+  int64_t expect = -1;
+  for (int d = ndim - 2; d >= 0; --d) {
+    if (sizes[d] == 1) continue;
+    if (expect < 0) {
+      expect = st[d];
+      *row_stride = st[d];
+    } else if (st[d] != expect) {
+      return false;
+    }
+    expect *= sizes[d];
+  }
+  if (expect < 0) *row_stride = 0;  // a single row
+  return true;
+}
+
 template <int OP>
 int binary_entry(const void* a, const int64_t* sa, const void* b, const int64_t* sb,
                  void* out, const int64_t* sizes, int ndim, double alpha, int dtype,
@@ -314,6 +407,14 @@ int binary_entry(const void* a, const int64_t* sa, const void* b, const int64_t*
       const bool all_aligned = aligned16(ap) && aligned16(bp) && aligned16(op);
       const bool a_dense = dense_strides(sz, sa_, ndim);
       const bool b_dense = dense_strides(sz, sb_, ndim);
+      if (a_dense && b_dense && n % (2 * VW) == 0 && aligned32(ap) && aligned32(bp) &&
+          aligned32(op)) {
+        const int64_t npk32 = n / (2 * VW);
+        binary_dense32_kernel<T, OP>
+            <<<full_grid(ceil_div(npk32, (int64_t)kBlock32 * kPacks32)), kBlock32, 0, stream>>>(
+                ap, bp, op, npk32, al);
+        return launch_status();
+      }
       if (a_dense && b_dense && n % VW == 0 && all_aligned) {
         auto kern = binary_dense_kernel<T, OP>;
         const int64_t npk = n / VW;
@@ -322,20 +423,30 @@ int binary_entry(const void* a, const int64_t* sa, const void* b, const int64_t*
         return launch_status();
       }
       const int64_t cols = ndim ? sz[ndim - 1] : 1;
-      if (ndim >= 1 && cols % VW == 0 && all_aligned) {
-        const bool b_row = a_dense && rowvec_strides(sz, sb_, ndim);
-        const bool a_row = b_dense && rowvec_strides(sz, sa_, ndim);
-        if (b_row || a_row) {
-          const int64_t npk = n / VW;
-          if (b_row) {
-            auto kern = binary_rowvec_kernel<T, OP, false>;
-            kern<<<grid_for(kern, npk, dev), kBlock, 0, stream>>>(ap, bp, op, npk,
-                                                                  cols / VW, al);
-          } else {
-            auto kern = binary_rowvec_kernel<T, OP, true>;
-            kern<<<grid_for(kern, npk, dev), kBlock, 0, stream>>>(bp, ap, op, npk,
-                                                                  cols / VW, al);
-          }
+      if (ndim >= 1 && cols % VW == 0 && aligned16(op)) {
+        const int64_t rows = n / cols, cpk = cols / VW;
+        const int grid = full_grid(ceil_div(rows, kTileRows));
+        int64_t rs = 0;
+        // full op v[c] / v[c] op full (v 16-byte aligned)
+        if (a_dense && aligned16(ap) && aligned16(bp) && rowvec_strides(sz, sb_, ndim)) {
+          binary_bcast_rows_kernel<T, OP, kRowVec, false>
+              <<<grid, kBlock, 0, stream>>>(ap, bp, 0, op, rows, cpk, al);
+          return launch_status();
+        }
+        if (b_dense && aligned16(ap) && aligned16(bp) && rowvec_strides(sz, sa_, ndim)) {
+          binary_bcast_rows_kernel<T, OP, kRowVec, true>
+              <<<grid, kBlock, 0, stream>>>(bp, ap, 0, op, rows, cpk, al);
+          return launch_status();
+        }
+        // full op s[r] / s[r] op full (one value per row, any alignment)
+        if (a_dense && aligned16(ap) && colvec_strides(sz, sb_, ndim, &rs)) {
+          binary_bcast_rows_kernel<T, OP, kColVec, false>
+              <<<grid, kBlock, 0, stream>>>(ap, bp, rs, op, rows, cpk, al);
+          return launch_status();
+        }
+        if (b_dense && aligned16(bp) && colvec_strides(sz, sa_, ndim, &rs)) {
+          binary_bcast_rows_kernel<T, OP, kColVec, true>
+              <<<grid, kBlock, 0, stream>>>(bp, ap, rs, op, rows, cpk, al);
           return launch_status();
         }
       }

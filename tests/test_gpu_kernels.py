@@ -322,7 +322,17 @@ def test_add_mul_fixtures(golden):
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("sa,sb", [((64, 4096), (64, 4096)), ((64, 4096), (4096,)),
                                    ((4096,), (64, 4096)), ((8, 1, 16), (1, 5, 16)),
-                                   ((3, 7), (3, 1)), ((2, 3, 4, 5), (5,)), ((1,), (9, 9))])
+                                   ((3, 7), (3, 1)), ((2, 3, 4, 5), (5,)), ((1,), (9, 9)),
+                                   # dense, not whole 32-byte packs: the 16-byte kernel
+                                   ((3, 1000), (3, 1000)),
+                                   # one value per row, second or first operand,
+                                   # whole and partial 8-row tiles, long rows
+                                   ((64, 4096), (64, 1)), ((64, 1), (64, 4096)),
+                                   ((13, 1024), (13, 1)), ((3, 8192), (1024 * 8,)),
+                                   # per-row values of a 3-d tensor (leading dims
+                                   # collapse to one stride) and ones that do not
+                                   # collapse (the N-d path)
+                                   ((4, 16, 256), (4, 16, 1)), ((4, 16, 256), (4, 1, 1))])
 def test_add_mul_broadcast(dtype, sa, sb):
     a, b = rnd(sa, dtype, 27), rnd(sb, dtype, 28)
     dt = parity.dname(dtype)

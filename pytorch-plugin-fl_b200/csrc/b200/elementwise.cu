@@ -225,6 +225,36 @@ scalar_float_vec_kernel(const T* a, T* o, int64_t npk, float s, float alpha) {
     st_stream(o + i * VW, pack<T>(x));
   }
 }
+// Two 32-byte packs per thread, 512-thread CTAs (as binary_dense32_kernel),
+// for 32-byte aligned tensors.
+template <typename T, int OP>
+__global__ void __launch_bounds__(kBlock32)
+scalar_float_vec32_kernel(const T* a, T* o, int64_t npk32, float s, float alpha) {
+  constexpr int VW = Elem<T>::kVec;
+  const int64_t i0 = (int64_t)blockIdx.x * (kBlock32 * kPacks32) + threadIdx.x;
+  Pack32 av[kPacks32];
+#pragma unroll
+  for (int k = 0; k < kPacks32; ++k) {
+    const int64_t i = i0 + (int64_t)k * kBlock32;
+    if (i < npk32) av[k] = ld_stream32(a + i * 2 * VW);
+  }
+#pragma unroll
+  for (int k = 0; k < kPacks32; ++k) {
+    const int64_t i = i0 + (int64_t)k * kBlock32;
+    if (i >= npk32) continue;
+    float x[VW];
+    Pack32 r;
+    unpack<T>(av[k].lo, x);
+#pragma unroll
+    for (int e = 0; e < VW; ++e) x[e] = apply_f<OP>(x[e], s, alpha);
+    r.lo = pack<T>(x);
+    unpack<T>(av[k].hi, x);
+#pragma unroll
+    for (int e = 0; e < VW; ++e) x[e] = apply_f<OP>(x[e], s, alpha);
+    r.hi = pack<T>(x);
+    st_stream32(o + i * 2 * VW, r);
+  }
+}
 template <typename I, int OP>
 __global__ void __launch_bounds__(kBlock)
 scalar_int_kernel(const I* a, I* o, int64_t n, I s, I alpha) {
@@ -280,6 +310,8 @@ __global__ void __launch_bounds__(kBlock) cast_kernel(const S* src, D* dst, int6
   }
   for (; i < n; i += nth) dst[i] = convert<S, D>(src[i]);
 }
+
+
 
 // 8 elements per thread per step through 16-byte accesses (both sides
 // aligned and n % 8 == 0).
@@ -517,7 +549,12 @@ FL_B200_API int fl_b200_binary_scalar(const void* a, double s, void* out, int64_
                                                            (T)(int64_t)alpha);
       } else {
         constexpr int VW = Elem<T>::kVec;
-        if (n % VW == 0 && aligned16(ap) && aligned16(outp)) {
+        if (n % (2 * VW) == 0 && aligned32(ap) && aligned32(outp)) {
+          const int64_t npk32 = n / (2 * VW);
+          scalar_float_vec32_kernel<T, OP>
+              <<<full_grid(ceil_div(npk32, (int64_t)kBlock32 * kPacks32)), kBlock32, 0, cs>>>(
+                  ap, outp, npk32, (float)s, (float)alpha);
+        } else if (n % VW == 0 && aligned16(ap) && aligned16(outp)) {
           auto kern = scalar_float_vec_kernel<T, OP>;
           kern<<<grid_for(kern, n / VW, dev), kBlock, 0, cs>>>(ap, outp, n / VW, (float)s,
                                                                (float)alpha);

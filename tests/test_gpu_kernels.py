@@ -364,6 +364,35 @@ def test_binary_scalar_keeps_opmath():
     parity.assert_ulp(got, ops.mul_golden(parity.to_np(x), 3.0, "bf16"), "bf16", 0, "mul scalar")
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("n", [4096 * 3 + 16, 1000, 1 << 20])
+def test_binary_scalar_vector_paths(dtype, n):
+    # whole 32-byte packs: two per thread in 512-thread CTAs (a partial last
+    # CTA at 12304 elements); 1000 16-bit values: the 16-byte kernel
+    x = rnd((n,), dtype, 34)
+    dt = parity.dname(dtype)
+    xn = parity.to_np(x).astype(np.float32)
+    got = parity.to_np(K.binary_scalar(x, 0.37, "add"))
+    parity.assert_ulp(got, ops.round_to(xn + np.float32(0.37), dt), dt, 0, "add scalar")
+    got = parity.to_np(K.binary_scalar(x, -1.7, "mul"))
+    parity.assert_ulp(got, ops.round_to(xn * np.float32(-1.7), dt), dt, 0, "mul scalar")
+
+
+@pytest.mark.parametrize("n", [12000, 8 * 1024 * 2, 1 << 20])
+def test_cast_vector_paths(n):
+    # n % 8 == 0 with 16-byte aligned tensors: two units of 8 per thread
+    # (a partial last CTA at 12000); every pair against torch's CPU cast
+    base = torch.randn(n, generator=torch.Generator().manual_seed(33)) * 1000
+    kinds = [torch.float32, torch.bfloat16, torch.float16, torch.int32, torch.int64]
+    for s in kinds:
+        src = base.to(s)
+        for d in kinds:
+            if d == s:
+                continue
+            got = K.cast(src.to(DEV), d).cpu()
+            assert torch.equal(got, src.to(d)), (n, s, d)
+
+
 def test_cast_all_pairs():
     vals = torch.tensor([0.0, -0.0, 1.0, -2.5, 65504.0, 1e-8, 3.14159, -1000.75, 7.0, 2**24 + 1.0])
     for s in [torch.float32, torch.bfloat16, torch.float16, torch.int32, torch.int64]:

@@ -355,6 +355,94 @@ softmax_loop_kernel(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
   }
 }
 
+// Rows longer than the register ladder (more than 4096 packs, e.g. a
+// vocabulary of 128256 logits), 16-byte aligned: one CTA of 512 threads per
+// row, grid-stride over rows.  Pass 1 reads the row once with 16-byte loads
+// (kLongUnroll packs per thread in flight), keeping a running max and a sum
+// rescaled when the max rises (x - m first, so a row at the lowest finite
+// value needs no special case there); the CTA combines the threads' (max,
+// sum); pass 2 reads the row again, from L2 when the rows in flight fit
+// there, and writes the probabilities.  Causal rows read their visible keys
+// only and store zeros past them.
+constexpr int kLongBlock = 512;
+constexpr int kLongUnroll = 4;
+
+template <typename TI, typename TO, bool CAUSAL>
+__global__ void __launch_bounds__(kLongBlock, 2)
+softmax_long_kernel(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows, int64_t cols,
+                    int64_t q_len, int64_t offset) {
+  constexpr int VW = Elem<TI>::kVec;
+  constexpr int U = kLongUnroll;
+  __shared__ float smem[kLongBlock / 32];
+  const int64_t nvec = cols / VW;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    int64_t nvalid = cols;
+    if (CAUSAL) nvalid = max((int64_t)0, min(cols, (row % q_len) + offset + 1));
+    const int64_t nv = CAUSAL ? ceil_div(nvalid, (int64_t)VW) : nvec;  // packs with a key
+    const TI* xr = x + row * ldx;
+    const auto masked = [&](uint4 v, int64_t p) {
+      if (CAUSAL && p * VW + VW > nvalid) v = mask_tail<TI>(v, (int)(nvalid - p * VW));
+      return v;
+    };
+    float m = -INFINITY, s = 0.f;
+    const auto consume = [&](uint4 v) {
+      const float pm = pack_max<TI>(v);
+      if (pm > m) {
+        s = (m == -INFINITY) ? 0.f : s * ex2_approx((m - pm) * kLog2e);
+        m = pm;
+      }
+      if (m != -INFINITY) {
+        float f[VW];
+        unpack<TI>(v, f);
+#pragma unroll
+        for (int e = 0; e < VW; ++e) s += ex2_approx((f[e] - m) * kLog2e);
+      }
+    };
+    int64_t p = threadIdx.x;
+    for (; p + (U - 1) * kLongBlock < nv; p += U * kLongBlock) {
+      uint4 v[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k) v[k] = ld_stream(xr + (p + k * kLongBlock) * VW);
+#pragma unroll
+      for (int k = 0; k < U; ++k) consume(masked(v[k], p + k * kLongBlock));
+    }
+    for (; p < nv; p += kLongBlock) consume(masked(ld_stream(xr + p * VW), p));
+    const float mrow = block_reduce<FastMaxOp, kLongBlock>(m, smem);
+    // each thread's sum rescaled to the row max (empty partials add 0)
+    const float part = (m == -INFINITY) ? 0.f : s * ex2_approx((m - mrow) * kLog2e);
+    const float srow = block_reduce<SumOp, kLongBlock>(part, smem);
+    const float inv = nvalid > 0 ? 1.0f / srow : __int_as_float(0x7fc00000);
+    const RowShift sh(mrow);
+    TO* yr = y + row * ldy;
+    const auto emit = [&](uint4 v, int64_t q) {
+      float o[VW];
+      if (!CAUSAL || q < nv) {
+        float f[VW];
+        unpack<TI>(masked(v, q), f);
+#pragma unroll
+        for (int e = 0; e < VW; ++e) o[e] = sh.exp(f[e]) * inv;
+      } else {
+#pragma unroll
+        for (int e = 0; e < VW; ++e) o[e] = 0.f * inv;
+      }
+      store_vals<TO, VW, false>(yr + q * VW, o);
+    };
+    int64_t q = threadIdx.x;
+    for (; q + (U - 1) * kLongBlock < nvec; q += U * kLongBlock) {
+      uint4 v[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        const int64_t qk = q + k * kLongBlock;
+        v[k] = (!CAUSAL || qk < nv) ? ld_stream(xr + qk * VW) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int k = 0; k < U; ++k) emit(v[k], q + k * kLongBlock);
+    }
+    for (; q < nvec; q += kLongBlock)
+      emit((!CAUSAL || q < nv) ? ld_stream(xr + q * VW) : make_uint4(0, 0, 0, 0), q);
+  }
+}
+
 // Softmax over the middle dim of a dense [outer, n, inner] view: one thread
 // per (outer, inner) column, three passes over n (coalesced across inner).
 template <typename TI, typename TO>
@@ -414,6 +502,14 @@ int launch_softmax(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
     }
     if (r < 0) r = row_ladder<8>(nvec, go);
     if (r >= 0) return r;
+    // longer rows: two CTAs per SM when their rows fit in 64 MB of L2 (pass
+    // 2 then re-reads from L2), else one
+    const int64_t row_bytes = cols * (int64_t)sizeof(TI);
+    const int per_sm = row_bytes * 2 * dev.sm_count <= (int64_t)64 << 20 ? 2 : 1;
+    const int grid = (int)std::min<int64_t>(rows, (int64_t)per_sm * dev.sm_count);
+    softmax_long_kernel<TI, TO, CAUSAL>
+        <<<grid, kLongBlock, 0, stream>>>(x, ldx, y, ldy, rows, cols, q_len, offset);
+    return launch_status();
   }
   auto kern = softmax_loop_kernel<TI, TO, CAUSAL>;
   static const int per_sm = blocks_per_sm(kern, 256, 0);

@@ -452,10 +452,10 @@ def test_causal_softmax(L, offset):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("cols", [512, 1024, 2048, 4096, 8192, 16384])
+@pytest.mark.parametrize("cols", [512, 1024, 2048, 4096, 8192, 16384, 65536])
 def test_softmax_row_rungs(dtype, cols):
     """Every rung of the register-row ladder from 512 to 16384 keys (4..128
-    threads per row, up to 8 packs per thread, and the looped kernel beyond),
+    threads per row, up to 8 packs per thread) and the two-pass kernel beyond,
     a ragged last group of rows, causal rows with a partly visible last pack
     and a history offset (the causal kernel runs only its visible pack
     iterations), fp32 output, and rows with a leading stride."""
@@ -472,6 +472,9 @@ def test_softmax_row_rungs(dtype, cols):
         got = K.softmax(xc, causal=True, causal_offset=off)
         ref = ops.softmax_golden(parity.to_np(xc), dt, causal=True, offset=off)
         check_float(got, ref, dt, f"causal {cols} off={off}")
+    # rows with no visible key (a negative offset) are all NaN
+    got = K.softmax(xc, causal=True, causal_offset=-3)
+    assert torch.isnan(got[:, :3]).all() and not torch.isnan(got[:, 3:]).any()
 
 
 @pytest.mark.parametrize("causal", [False, True])

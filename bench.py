@@ -847,6 +847,7 @@ PROFILE_CASES = {
     "swiglu_backward": "SwiGLU backward bf16 [4096, 14336]",
     "softmax_backward": "softmax backward bf16 [2, 32, 2048, 2048]",
     "masked_softmax": "scaled masked softmax bf16 [2, 32, 2048, 2048], HF mask [2, 1, 2048, 2048]",
+    "softmax_long": "softmax bf16 [512, 128256] (a vocabulary of logits per row)",
 }
 
 
@@ -880,6 +881,9 @@ def profile_case(name):
         gt, up, d = (torch.randn(4096, INTER, generator=g, device=dev).to(torch.bfloat16)
                      for _ in range(3))
         fn = lambda: K.swiglu_backward(d, gt, up)  # noqa: E731
+    elif name == "softmax_long":
+        x = (3.0 * torch.randn(512, 128256, generator=g, device=dev)).to(torch.bfloat16)
+        fn = lambda: K.softmax(x)  # noqa: E731
     elif name == "masked_softmax":
         x = (3.0 * torch.randn(2, 32, 2048, 2048, generator=g, device=dev)).to(torch.bfloat16)
         m = torch.zeros(2, 1, 2048, 2048, dtype=torch.bfloat16, device=dev).masked_fill(

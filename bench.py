@@ -848,6 +848,8 @@ PROFILE_CASES = {
     "softmax_backward": "softmax backward bf16 [2, 32, 2048, 2048]",
     "masked_softmax": "scaled masked softmax bf16 [2, 32, 2048, 2048], HF mask [2, 1, 2048, 2048]",
     "softmax_long": "softmax bf16 [512, 128256] (a vocabulary of logits per row)",
+    "elementwise": "add bf16 [32768, 4096] + [32768, 4096]; mul by a [4096] row vector; "
+                   "mul by a [32768, 1] column",
 }
 
 
@@ -881,6 +883,12 @@ def profile_case(name):
         gt, up, d = (torch.randn(4096, INTER, generator=g, device=dev).to(torch.bfloat16)
                      for _ in range(3))
         fn = lambda: K.swiglu_backward(d, gt, up)  # noqa: E731
+    elif name == "elementwise":
+        a = torch.randn(32768, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+        b = torch.randn(32768, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+        wv = torch.randn(HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+        cv = torch.randn(32768, 1, generator=g, device=dev).to(torch.bfloat16)
+        fn = lambda: (K.add(a, b), K.mul(a, wv), K.mul(a, cv))  # noqa: E731
     elif name == "softmax_long":
         x = (3.0 * torch.randn(512, 128256, generator=g, device=dev)).to(torch.bfloat16)
         fn = lambda: K.softmax(x)  # noqa: E731

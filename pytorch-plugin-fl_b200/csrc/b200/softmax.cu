@@ -36,6 +36,17 @@ __device__ __forceinline__ float exp_shifted(float x, float mlog2e) {
   return ex2_approx(fmaf(x, kLog2e, -mlog2e));
 }
 
+// Pair k of a 16-byte pack as fp32 (elements 2k and 2k+1).
+template <typename T>
+__device__ __forceinline__ uint64_t pack_pair(const uint4& v, int k) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  if constexpr (std::is_same<T, float>::value) {
+    return f2_make(__uint_as_float(w[2 * k]), __uint_as_float(w[2 * k + 1]));
+  } else {
+    return pair_from_bits<T>(w[k]);
+  }
+}
+
 // A row max too far below zero for the one-FMA exp: m*log2e overflows to
 // -inf for a finite m below -2.36e38, e.g. a row whose every key is masked
 // with the lowest finite value (HF's additive attention mask for a padding
@@ -57,8 +68,10 @@ __device__ __forceinline__ uint4 shift_pack(const uint4& v, float m) {
   return pack<T>(f);
 }
 
-// The same for the looped kernels, which read the row again instead of
-// keeping it: exp(x - m) in the one-FMA form, or x - m first for a wide row.
+// The same for the middle-dim kernel, which reads its column again instead
+// of keeping it: exp(x - m) in the one-FMA form, or x - m first for a wide
+// row.  Its sum and its outputs take the same form, so the factor
+// 2^(rounding error of m*log2e) common to a row's exps cancels.
 struct RowShift {
   float m, ml;
   bool wide;
@@ -343,11 +356,12 @@ softmax_loop_kernel(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
     const float part = (m == -INFINITY) ? 0.f : s * exp2f((m - mrow) * kLog2e);
     const float srow = block_reduce<SumOp, 256>(part, smem);
     const float inv = nvalid > 0 ? 1.0f / srow : __int_as_float(0x7fc00000);
-    const RowShift sh(mrow);
     TO* yr = y + row * ldy;
+    // the argument the sum was taken of, (x - m) * log2e (see the two-pass
+    // kernel below for why not the one-FMA form)
     for (int64_t c = threadIdx.x; c < cols; c += 256) {
       float o;
-      if (c < nvalid) o = sh.exp(Elem<TI>::to_f(xr[c])) * inv;
+      if (c < nvalid) o = ex2_approx((Elem<TI>::to_f(xr[c]) - mrow) * kLog2e) * inv;
       else o = nvalid > 0 ? 0.f : inv;
       if constexpr (std::is_same<TO, float>::value) yr[c] = o;
       else yr[c] = Elem<TO>::from_f(o);
@@ -386,18 +400,24 @@ softmax_long_kernel(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows, 
       if (CAUSAL && p * VW + VW > nvalid) v = mask_tail<TI>(v, (int)(nvalid - p * VW));
       return v;
     };
-    float m = -INFINITY, s = 0.f;
+    constexpr int NP = VW / 2;  // fp32 pairs per pack
+    const uint64_t log2e2 = f2_make(kLog2e, kLog2e);
+    float m = -INFINITY;
+    uint64_t s2 = f2_make(0.f, 0.f);  // the thread's running sum, in two lanes
     const auto consume = [&](uint4 v) {
       const float pm = pack_max<TI>(v);
       if (pm > m) {
-        s = (m == -INFINITY) ? 0.f : s * ex2_approx((m - pm) * kLog2e);
+        const float r = (m == -INFINITY) ? 0.f : ex2_approx((m - pm) * kLog2e);
+        s2 = f2_mul(s2, f2_make(r, r));
         m = pm;
       }
       if (m != -INFINITY) {
-        float f[VW];
-        unpack<TI>(v, f);
+        const uint64_t nm2 = f2_make(-m, -m);
 #pragma unroll
-        for (int e = 0; e < VW; ++e) s += ex2_approx((f[e] - m) * kLog2e);
+        for (int k = 0; k < NP; ++k) {
+          const uint64_t t = f2_mul(f2_add(pack_pair<TI>(v, k), nm2), log2e2);
+          s2 = f2_add(s2, f2_make(ex2_approx(f2_lo(t)), ex2_approx(f2_hi(t))));
+        }
       }
     };
     int64_t p = threadIdx.x;
@@ -411,18 +431,30 @@ softmax_long_kernel(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows, 
     for (; p < nv; p += kLongBlock) consume(masked(ld_stream(xr + p * VW), p));
     const float mrow = block_reduce<FastMaxOp, kLongBlock>(m, smem);
     // each thread's sum rescaled to the row max (empty partials add 0)
+    const float s = f2_lo(s2) + f2_hi(s2);
     const float part = (m == -INFINITY) ? 0.f : s * ex2_approx((m - mrow) * kLog2e);
     const float srow = block_reduce<SumOp, kLongBlock>(part, smem);
     const float inv = nvalid > 0 ? 1.0f / srow : __int_as_float(0x7fc00000);
-    const RowShift sh(mrow);
+    const uint64_t nmrow2 = f2_make(-mrow, -mrow), inv2 = f2_make(inv, inv);
     TO* yr = y + row * ldy;
+    // Pass 2: every output from ex2.approx (exact zeros below its range) of
+    // (x - m) * log2e, the argument pass 1 summed: the one-FMA form
+    // x*log2e - round(m*log2e) would scale every output by 2^(rounding error
+    // of m*log2e), up to 2^(|m| * 2^-24), which the sum of pass 1 does not
+    // share (0.15 % for a row at the fp16 lowest value).  x - m is exact near
+    // the max, also for a max below -2.36e38, so no row needs a shift first.
+    // Adds and multiplies in pairs, rounded lane by lane as the scalar ones.
     const auto emit = [&](uint4 v, int64_t q) {
       float o[VW];
       if (!CAUSAL || q < nv) {
-        float f[VW];
-        unpack<TI>(masked(v, q), f);
+        const uint4 u = masked(v, q);
 #pragma unroll
-        for (int e = 0; e < VW; ++e) o[e] = sh.exp(f[e]) * inv;
+        for (int k = 0; k < NP; ++k) {
+          const uint64_t t = f2_mul(f2_add(pack_pair<TI>(u, k), nmrow2), log2e2);
+          const uint64_t r = f2_mul(f2_make(ex2_approx(f2_lo(t)), ex2_approx(f2_hi(t))), inv2);
+          o[2 * k] = f2_lo(r);
+          o[2 * k + 1] = f2_hi(r);
+        }
       } else {
 #pragma unroll
         for (int e = 0; e < VW; ++e) o[e] = 0.f * inv;

@@ -499,6 +499,40 @@ def test_softmax_f32_out_both_store_widths(causal):
         assert torch.isnan(buf[:shift]).all() and torch.isnan(buf[shift + rows * cols:]).all()
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("cols", [40000, 131072, 40001])
+def test_softmax_long_rows_special_values(dtype, cols):
+    """The two-pass kernel (rows over 4096 packs, both block sizes; 40001
+    columns take the unaligned loop kernel, also two passes) with -inf
+    keys, keys far below the max, a one-hot row, a row at the format's
+    lowest finite value (fp16 -65504: pass 2 must use the argument pass 1
+    summed, else the rounding of m*log2e scales every output by up to
+    2^(|m| * 2^-24)), and a NaN or an all -inf row, which come out all NaN."""
+    dt = parity.dname(dtype)
+    g = torch.Generator().manual_seed(cols + 7)
+    x = 3.0 * torch.randn(8, cols, generator=g)
+    x[0, ::7] = float("-inf")
+    x[1] = -60.0 * torch.rand(cols, generator=g)
+    x[1, ::5] = -150.0
+    x[2] = float("-inf")
+    x[2, cols // 3] = 1.5
+    x[3] = torch.finfo(dtype).min
+    x[4, 12345] = float("nan")
+    x[5] = float("-inf")
+    x[6, : cols // 2] = float("-inf")          # the first half of the row masked
+    x = x.to(dtype).to(DEV)
+    got = K.softmax(x)
+    ref = ops.softmax_golden(parity.to_np(x), dt)
+    ok = [0, 1, 2, 3, 6, 7]
+    check_float(got[ok], ref[ok], dt, f"long {cols}")
+    assert torch.isnan(got[4]).all() and torch.isnan(got[5]).all()
+    assert got[2, cols // 3].item() == 1.0 and (got[2].float().sum() == 1.0).item()
+    if dtype != torch.float32:
+        got32 = K.softmax(x, out_dtype=torch.float32)
+        ref32 = ops.softmax_golden(parity.to_np(x), "f32")
+        parity.assert_rel(parity.to_np(got32[ok]), ref32[ok], rtol=1e-5, atol=1e-30)
+
+
 def test_softmax_infinities():
     x = torch.tensor([[float("-inf")] * 8, [0.0, float("-inf"), 1.0, float("-inf"), 2, 3, 4, 5],
                       [1.0, float("nan"), 2, 3, 4, 5, 6, 7], [float("inf"), 1, 2, 3, 4, 5, 6, 7]])

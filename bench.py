@@ -636,10 +636,27 @@ def main():
         # the e2e result equals the device-resident path's result
         same = bool(torch.equal(h_out.to(dev), stack.run(stack.x0)))
         nbytes = h_in.numel() * h_in.element_size()
+        # This box's plain pinned-copy rates, one direction at a time, after
+        # the timed region (the e2e step moves nbytes each way, so these set
+        # its floor: measured 1.48 M tokens/s on one box and 0.87 M on
+        # another with the same build and the same device-resident step).
+        tmp = torch.empty_like(stack.x0)
+        rates = {}
+        for name, dst, src in (("h2d", tmp, h_in), ("d2h", h_out, tmp)):
+            best = float("inf")
+            for _ in range(2):
+                c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                c0.record()
+                dst.copy_(src, non_blocking=True)
+                c1.record()
+                torch.cuda.synchronize()
+                best = min(best, c0.elapsed_time(c1))
+            rates[name] = round(nbytes / (best / 1e3) / 1e9, 1)
+        del tmp
         e2e = {"value": args.tokens * args.steps / (ems / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": nbytes * world, "d2h_bytes_per_step": nbytes * world,
                "ms_per_step": ems / args.steps, "matches_device_path": same,
-               "chunks": chunks,
+               "chunks": chunks, "host_copy_gbs": rates,
                "api": "torch_fl.ops (flagos:: ops) on flagos tensors, host<->flagos copies "
                       "on flagos streams overlapping the layers"}
 

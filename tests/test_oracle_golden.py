@@ -92,6 +92,35 @@ def test_softmax(golden):
                       what="dim0")
 
 
+def test_softmax_special_rows_match_torch():
+    """The oracle's softmax on the rows the long-row GPU test uses, against
+    torch's own fp64 softmax: -inf keys, keys far below the max, one-hot,
+    a row at each format's lowest finite value (uniform), and NaN / all -inf
+    rows (all NaN)."""
+    import torch
+
+    for dtype, dt in ((torch.float32, "f32"), (torch.bfloat16, "bf16"), (torch.float16, "f16")):
+        g = torch.Generator().manual_seed(3)
+        x = 3.0 * torch.randn(7, 4096, generator=g)
+        x[0, ::7] = float("-inf")
+        x[1] = -60.0 * torch.rand(4096, generator=g)
+        x[1, ::5] = -150.0
+        x[2] = float("-inf")
+        x[2, 100] = 1.5
+        x[3] = torch.finfo(dtype).min
+        x[4, 123] = float("nan")
+        x[5] = float("-inf")
+        x = x.to(dtype)
+        xn = parity.to_np(x)
+        ref = torch.softmax(x.double(), -1).numpy()
+        got = ops.softmax_golden(xn, "f32")
+        assert np.array_equal(np.isnan(got), np.isnan(ref)), dt
+        assert np.isnan(got[4]).all() and np.isnan(got[5]).all()
+        ok = [0, 1, 2, 3, 6]
+        parity.assert_rel(got[ok], ref[ok].astype(np.float32), rtol=1e-6, atol=1e-38, what=dt)
+        assert got[2, 100] == 1.0 and np.all(got[3] == np.float32(1.0 / 4096))
+
+
 def test_float_reductions(golden):
     x = golden.get("reduce_f32/x")
     # torch's own fp32 sums meet the stated sum tolerance against fp64

@@ -161,12 +161,23 @@ def rope_tables(positions, dim: int, theta: float, dtype: str):
     """cos/sin tables as HF builds them (Qwen3RotaryEmbedding,
     modeling_qwen3.py:86-148): inv_freq = 1/theta^(arange(0,D,2)/D) in fp32,
     freqs = pos * inv_freq (fp32), emb = cat(freqs, freqs), cos/sin in fp32,
-    then cast to the activation dtype."""
-    exps = np.arange(0, dim, 2, dtype=np.int64).astype(np.float32) / np.float32(dim)
-    inv_freq = (np.float32(1.0) / (np.float32(theta) ** exps)).astype(np.float32)
-    freqs = np.asarray(positions, np.float32)[:, None] * inv_freq[None, :]
-    emb = np.concatenate([freqs, freqs], axis=-1).astype(np.float32)
-    return round_to(np.cos(emb), dtype), round_to(np.sin(emb), dtype)
+    then cast to the activation dtype.
+
+    The fp32 steps run on torch CPU aten -- the kernels the reference's CPU
+    path uses -- because the table is defined by them: numpy's float32 power
+    and cos/sin differ from torch's in the last bit for some exponents and
+    angles, and a last-bit difference in inv_freq times a position near
+    131072 moves cos/sin by up to ~145 bf16 ulp.  The position product is an
+    elementwise fp32 multiply, which is what HF's [D/2, 1] @ [1, S] matmul
+    computes (one product per output, no sum)."""
+    import torch
+
+    inv_freq = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.int64).to(torch.float32) / dim))
+    pos = torch.as_tensor(np.asarray(positions, np.int64)).to(torch.float32)
+    freqs = pos[:, None] * inv_freq[None, :]
+    emb = torch.cat((freqs, freqs), dim=-1)
+    c, s = emb.cos().numpy(), emb.sin().numpy()
+    return round_to(c, dtype), round_to(s, dtype)
 
 
 # ------------------------------------------------------------------ SwiGLU ---

@@ -125,6 +125,31 @@ def main() -> None:
     _store(d, "qknorm_rope_bf16/q_out", qe.contiguous())
     _store(d, "qknorm_rope_bf16/k_out", ke.contiguous())
 
+    # --- RoPE at stack-scale positions (the 131072-token stack's last rows and
+    # the 2^16 boundary), where a last-bit difference in inv_freq is magnified
+    # by the position; tables from the transformers module itself.
+    pos_far = torch.tensor([[8191, 16383, 32767, 65535, 65536, 98304, 114688, 131070, 131071]],
+                           dtype=torch.int64)
+    Sf = pos_far.shape[1]
+    g = _gen(15)
+    qf_ = torch.randn(1, Sf, 32, 128, generator=g).to(torch.bfloat16).transpose(1, 2)
+    kf_ = torch.randn(1, Sf, 8, 128, generator=g).to(torch.bfloat16).transpose(1, 2)
+    with torch.no_grad():
+        cos_f, sin_f = rot(qf_, pos_far)
+        cos_f32, sin_f32 = rot(qf_.float(), pos_far)
+    c2, s2 = hf_chain.rope_tables(pos_far, 128, 10000.0, torch.bfloat16)
+    assert torch.equal(cos_f, c2) and torch.equal(sin_f, s2)
+    qe, ke = mq.apply_rotary_pos_emb(qf_, kf_, cos_f, sin_f)
+    _store(d, "rope_bf16_far/pos", pos_far)
+    _store(d, "rope_bf16_far/q", qf_.contiguous())
+    _store(d, "rope_bf16_far/k", kf_.contiguous())
+    _store(d, "rope_bf16_far/cos", cos_f)
+    _store(d, "rope_bf16_far/sin", sin_f)
+    _store(d, "rope_bf16_far/cos_f32", cos_f32)
+    _store(d, "rope_bf16_far/sin_f32", sin_f32)
+    _store(d, "rope_bf16_far/q_out", qe.contiguous())
+    _store(d, "rope_bf16_far/k_out", ke.contiguous())
+
     # --- SwiGLU, bf16 (act_fn = silu)
     g = _gen(3)
     gate = torch.randn(16, 1024, generator=g).to(torch.bfloat16)

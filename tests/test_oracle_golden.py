@@ -43,6 +43,32 @@ def test_rope_chain_bit_exact(golden):
     parity.assert_ulp(ops.rope_chain(k, cos, sin, "bf16"), golden.get("rope_bf16/k_out"), "bf16", 0, "k")
 
 
+@pytest.mark.parametrize("fixture", ["rope_bf16", "rope_bf16_far"])
+def test_rope_tables_are_hf_tables(golden, fixture):
+    # The oracle's cos/sin must be the transformers module's own tables, bit
+    # for bit, at the 8192-token config's positions and at stack-scale ones
+    # (up to 131071, where one ulp of inv_freq moves cos by ~145 bf16 ulp).
+    pos = golden.get(f"{fixture}/pos")[0]
+    c, s = ops.rope_tables(pos, 128, 1e4, "bf16")
+    parity.assert_ulp(c, golden.get(f"{fixture}/cos")[0], "bf16", 0, "cos")
+    parity.assert_ulp(s, golden.get(f"{fixture}/sin")[0], "bf16", 0, "sin")
+    if fixture == "rope_bf16_far":
+        c32, s32 = ops.rope_tables(pos, 128, 1e4, "f32")
+        assert np.array_equal(c32, golden.get(f"{fixture}/cos_f32")[0])
+        assert np.array_equal(s32, golden.get(f"{fixture}/sin_f32")[0])
+
+
+def test_rope_chain_bit_exact_far_positions(golden):
+    q, k = golden.get("rope_bf16_far/q"), golden.get("rope_bf16_far/k")
+    pos = golden.get("rope_bf16_far/pos")[0]
+    c, s = ops.rope_tables(pos, 128, 1e4, "bf16")
+    cos, sin = c[None, None], s[None, None]
+    parity.assert_ulp(ops.rope_chain(q, cos, sin, "bf16"), golden.get("rope_bf16_far/q_out"),
+                      "bf16", 0, "q")
+    parity.assert_ulp(ops.rope_chain(k, cos, sin, "bf16"), golden.get("rope_bf16_far/k_out"),
+                      "bf16", 0, "k")
+
+
 def test_rope_golden_is_the_single_rounding(golden):
     # The reference rounds three times (two products, one sum), so where the
     # sum cancels it is far, in ulps of the result, from the single-rounded

@@ -372,10 +372,10 @@ class EventTimer:
 
 
 # ----------------------------------------------------------- CPU reference
-def cpu_reference(sample_tokens, reps, threads):
+def cpu_reference(sample_tokens, reps, threads, warmup=1):
     """The reference's own CPU path on a bounded sample: one decoder layer's
     chain on `sample_tokens` tokens, HF formulas over torch CPU aten.  Returns
-    (seconds per token-layer, description)."""
+    (seconds per token-layer, description, median ms of one sample)."""
     from oracle import hf_chain
 
     torch.set_num_threads(threads)
@@ -391,18 +391,18 @@ def cpu_reference(sample_tokens, reps, threads):
     k = rn(1, T, HKV, HEAD).transpose(1, 2)
     gt, up = rn(T, INTER), rn(T, INTER)
     cos, sin = hf_chain.rope_tables(torch.arange(T)[None], HEAD, THETA, bf)
-    hf_chain.decoder_chain(x[:64], w, q[:, :, :64], k[:, :, :64], cos[:, :64], sin[:, :64],
-                           gt[:64], up[:64], y[:64], EPS)   # warm-up
+    for _ in range(max(warmup, 1)):
+        hf_chain.decoder_chain(x, w, q, k, cos, sin, gt, up, y, EPS)
     times = []
     for _ in range(reps):
         t0 = time.perf_counter()
         hf_chain.decoder_chain(x, w, q, k, cos, sin, gt, up, y, EPS)
         times.append(time.perf_counter() - t0)
-    per = statistics.median(times) / T
+    med = statistics.median(times)
     desc = (f"HF formulas (modeling_qwen3.py RMSNorm/apply_rotary_pos_emb/silu*up) + add on torch "
             f"{torch.__version__} CPU aten, one decoder layer x {T} tokens, median of {reps}; "
-            f"scaled to the 32-layer stack")
-    return per, desc
+            f"extrapolated to the 32-layer stack by tokens x layers")
+    return med / T, desc, med * 1e3
 
 
 def cpu_info():
@@ -418,6 +418,15 @@ def cpu_info():
     return model
 
 
+def workload_config(args, world):
+    """The workload both arms run (the same dict on the b200 and the
+    reference line)."""
+    return {"workload": WORKLOAD, "tokens": args.tokens, "tokens_per_rank": args.tokens // world,
+            "layers": args.layers, "hidden": HIDDEN, "intermediate": INTER,
+            "heads": [HQ, HKV, HEAD], "parallelism": f"rows/{world}",
+            "l2": "inputs larger than L2 (every per-rank activation >= 256 MB)"}
+
+
 # --------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -429,7 +438,9 @@ def main():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--rounding", default="fused", choices=["fused", "chain"])
     ap.add_argument("--no-fuse-add-norm", action="store_true")
-    ap.add_argument("--cpu-sample-tokens", type=int, default=2048)
+    # one layer of the 8192-token chain: the rate per token of a smaller,
+    # cache-resident sample is higher (2048 tokens: 1.7x on one host)
+    ap.add_argument("--cpu-sample-tokens", type=int, default=8192)
     ap.add_argument("--cpu-reps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -460,15 +471,23 @@ def main():
         if rank != 0:
             return
         reps = max(args.steps, 1)
-        per, desc = cpu_reference(args.cpu_sample_tokens, reps, threads)
+        per, desc, sample_ms = cpu_reference(args.cpu_sample_tokens, reps, threads,
+                                             warmup=args.warmup)
         value = 1.0 / (per * args.layers)
+        # Each step times one decoder layer of the chain on `sample_tokens`
+        # tokens (BASELINE's 8192-token chain by default); the stack's rate is
+        # that per-token-layer time scaled to `layers` layers.  ms_per_step is
+        # the time of the step actually run; the full stack's time per step
+        # is given under its own key.
         line = {"metric": "fused-layer tokens/s", "value": value, "unit": "tokens/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": per * args.tokens * args.layers * 1e3, "higher_is_better": True,
+                "ms_per_step": sample_ms, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "impl": "reference",
-                "config": {"workload": WORKLOAD, "tokens": args.tokens, "layers": args.layers,
-                           "hidden": HIDDEN, "intermediate": INTER, "heads": [HQ, HKV, HEAD]},
+                "impl": "reference", "extrapolated": True,
+                "sample_tokens": args.cpu_sample_tokens, "sample_layers": 1,
+                "sample_ms_median": sample_ms,
+                "ms_per_step_extrapolated": per * args.tokens * args.layers * 1e3,
+                "config": workload_config(args, world),
                 "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads,
                                  "kind": "reference", "sample": desc, "cpu": cpu_info()},
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -700,7 +719,7 @@ def main():
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            per, desc = cpu_reference(args.cpu_sample_tokens, args.cpu_reps, threads)
+            per, desc, _ = cpu_reference(args.cpu_sample_tokens, args.cpu_reps, threads)
             cpu = {"value": 1.0 / (per * args.layers), "unit": "tokens/s", "cores": threads,
                    "kind": "reference", "sample": desc, "cpu": cpu_info()}
         line = {
@@ -708,14 +727,11 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "tokens": args.tokens, "tokens_per_rank": T,
-                       "layers": args.layers, "hidden": HIDDEN, "intermediate": INTER,
-                       "heads": [HQ, HKV, HEAD], "rounding": args.rounding,
-                       "fused_add_rms_norm": not args.no_fuse_add_norm,
-                       "parallelism": f"rows/{world}",
-                       "launch": "CUDA graph replay of the step" if not args.no_graph
-                                 else "eager launches",
-                       "l2": "inputs larger than L2 (every per-rank activation >= 256 MB)"},
+            "config": workload_config(args, world),
+            "impl_config": {"rounding": args.rounding,
+                            "fused_add_rms_norm": not args.no_fuse_add_norm,
+                            "launch": "CUDA graph replay of the step" if not args.no_graph
+                                      else "eager launches"},
             "hbm_gbs_step": round(stack_bytes(stack) * args.steps / (ms / 1e3) / 1e9, 1),
             "per_op": per_op, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_eager_reference": eager, "per_op_configs": per_op_configs,
@@ -739,13 +755,18 @@ def op_configs(dev, peak, reps=5):
     out = {}
     g = torch.Generator(device=dev).manual_seed(7)
 
-    def timed(name, fn, nbytes, note=""):
+    # written before every timed rep of a case whose inputs L2 could hold
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def timed(name, fn, nbytes, note="", flush=False, tokens=None, reps_=None):
         for _ in range(2):
             fn()
         torch.cuda.synchronize()
         ts = []
-        for _ in range(reps):
+        for _ in range(reps_ or reps):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            if flush:
+                flush_buf.fill_(1)   # 256 MB > L2: the inputs come from HBM
             # A bounded spin kernel keeps the GPU busy while the host prepares
             # the launch, so the events bracket the op's device time only.
             torch.cuda._sleep(2_000_000)
@@ -758,8 +779,14 @@ def op_configs(dev, peak, reps=5):
         gbs = nbytes / (ms * 1e-3) / 1e9
         out[name] = {"ms": round(ms, 4), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
                      "bytes": int(nbytes)}
+        if tokens:
+            out[name]["tokens_per_s"] = round(tokens / (ms * 1e-3), 1)
+        if flush:
+            out[name]["l2"] = "256 MB written before each rep"
         if note:
             out[name]["note"] = note
+
+    chain_configs(dev, g, timed)
 
     # config 1: RMSNorm fp32 [2048, 4096], eps 1e-6
     x = torch.randn(2048, 4096, generator=g, device=dev)
@@ -848,6 +875,119 @@ def op_configs(dev, peak, reps=5):
     del lg, yb, dyb
     torch.cuda.empty_cache()
     return out
+
+
+def chain_configs(dev, g, timed, T=8192):
+    """The Llama decoder chain at 8192 tokens on one GPU: RMSNorm(4096, eps
+    1e-5) -> RoPE (q [T,32,128], k [T,8,128], theta 1e4, positions 0..T-1) ->
+    SwiGLU [T,14336] -> residual add, inputs ~ N(0,1), weight 1 + N(0,0.1).
+    Timed as one step four ways: the four b200 launches replayed as a CUDA
+    graph; the same launches eager; three launches (SwiGLU and the residual
+    add in one kernel) as a graph; the HF formulas on PyTorch's CUDA kernels
+    (what the reference's cuda route runs).  Bytes: 147,456 per token plus
+    the cos/sin rows (512 per token).  Also the Qwen3 q/k-norm -> RoPE
+    (rms_norm_rope) at the same token count, 20,480 B/token."""
+    from torch_fl import kernels as K
+
+    bf = torch.bfloat16
+
+    def rn(*shape, scale=1.0, loc=0.0):
+        return (loc + scale * torch.randn(*shape, generator=g, device=dev)).to(bf)
+
+    x, y = rn(T, HIDDEN), rn(T, HIDDEN)
+    w = rn(HIDDEN, scale=0.1, loc=1.0)
+    q, k = rn(1, T, HQ, HEAD), rn(1, T, HKV, HEAD)
+    gt, up = rn(T, INTER), rn(T, INTER)
+    cos, sin = rope_tables(0, T, dev)
+    n, h = torch.empty_like(x), torch.empty_like(x)
+    qo, ko, a = torch.empty_like(q), torch.empty_like(k), torch.empty_like(gt)
+
+    def rms():
+        K.rms_norm(x, w, EPS, out=n)
+
+    def rope():
+        K.rope_qk(q, k, cos, sin, layout="bshd", q_out=qo, k_out=ko)
+
+    def swi():
+        K.swiglu(gt, up, out=a)
+
+    def add():
+        K.add(x, y, out=h)
+
+    def chain4():
+        rms(); rope(); swi(); add()   # noqa: E702
+
+    def chain3():
+        rms(); rope()                 # noqa: E702
+        K.swiglu_residual(gt, up, x, y, act_out=a, h_out=h)
+
+    def graph_of(fn):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn()
+        torch.cuda.synchronize()
+        return gr
+
+    chain_bytes = (BYTES["rms_norm"] + BYTES["rope_qk"] + BYTES["swiglu"] + BYTES["residual_add"]
+                   + TABLE_BYTES_PER_TOKEN) * T
+    tag = f"llama_chain_T{T}"
+    g4, g3 = graph_of(chain4), graph_of(chain3)
+    timed(f"{tag}_graph", g4.replay, chain_bytes,
+          "RMSNorm, RoPE, SwiGLU, residual add: 4 b200 launches replayed as one CUDA graph",
+          flush=True, tokens=T, reps_=20)
+    timed(f"{tag}_eager", chain4, chain_bytes, "the same 4 launches, eager", flush=True,
+          tokens=T, reps_=20)
+    timed(f"{tag}_fused_graph", g3.replay, chain_bytes,
+          "RMSNorm, RoPE, SwiGLU+residual in one kernel: 3 launches as one CUDA graph",
+          flush=True, tokens=T, reps_=20)
+    del g4, g3
+
+    def torch_chain():
+        hf = x.to(torch.float32)
+        hf = hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + EPS)
+        nn = w * hf.to(bf)
+        qt, kt = q.transpose(1, 2), k.transpose(1, 2)
+        c, s_ = cos[None, None], sin[None, None]
+
+        def rot(t):
+            return torch.cat((-t[..., HEAD // 2:], t[..., :HEAD // 2]), dim=-1)
+
+        qe = (qt * c) + (rot(qt) * s_)
+        ke = (kt * c) + (rot(kt) * s_)
+        aa = torch.nn.functional.silu(gt) * up
+        return nn, qe, ke, aa, x + y
+
+    timed(f"{tag}_torch_eager", torch_chain, chain_bytes,
+          "HF formulas on PyTorch CUDA eager kernels (the reference's cuda route)", flush=True,
+          tokens=T, reps_=10)
+    # the chain's kernels one at a time at this size
+    timed(f"rms_norm_bf16_{T}x{HIDDEN}", rms, BYTES["rms_norm"] * T, flush=True, reps_=20)
+    timed(f"rope_qk_bf16_T{T}", rope, (BYTES["rope_qk"] + TABLE_BYTES_PER_TOKEN) * T, flush=True,
+          reps_=20)
+    timed(f"swiglu_bf16_{T}x{INTER}", swi, BYTES["swiglu"] * T, flush=True, reps_=20)
+    timed(f"add_bf16_{T}x{HIDDEN}", add, BYTES["residual_add"] * T, flush=True, reps_=20)
+    del gt, up, a, x, y, n, h
+    # Qwen3 q_norm / k_norm (per-head RMSNorm over 128, eps 1e-6, [128] weights)
+    # then RoPE, one launch; bytes: q, k read and written + the table rows
+    wq, wk = rn(HEAD, scale=0.1, loc=1.0), rn(HEAD, scale=0.1, loc=1.0)
+    nr_bytes = (BYTES["rope_qk"] + TABLE_BYTES_PER_TOKEN) * T
+    timed(f"rms_norm_rope_bf16_T{T}", lambda: K.rope_qk(
+        q, k, cos, sin, layout="bshd", q_weight=wq, k_weight=wk, eps=1e-6, q_out=qo, k_out=ko),
+        nr_bytes, "Qwen3-8B shapes: q [T,32,128], k [T,8,128], [128] norm weights", flush=True,
+        tokens=T, reps_=20)
+    TL = 131072
+    q2, k2 = rn(1, TL, HQ, HEAD), rn(1, TL, HKV, HEAD)
+    c2, s2 = rope_tables(0, TL, dev)
+    timed(f"rms_norm_rope_bf16_T{TL}", lambda: K.rope_qk(
+        q2, k2, c2, s2, layout="bshd", q_weight=wq, k_weight=wk, eps=1e-6, inplace=True),
+        (BYTES["rope_qk"] + TABLE_BYTES_PER_TOKEN) * TL, "in place, inputs larger than L2",
+        tokens=TL)
+    del q2, k2, c2, s2, q, k, qo, ko
 
 
 def stack_bytes(stack):

@@ -438,7 +438,9 @@ softmax_long_kernel(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows, 
     const uint64_t nmrow2 = f2_make(-mrow, -mrow), inv2 = f2_make(inv, inv);
     TO* yr = y + row * ldy;
     // Pass 2: every output from ex2.approx (exact zeros below its range) of
-    // (x - m) * log2e, the argument pass 1 summed: the one-FMA form
+    // (x - m) * log2e.  Pass 1 summed exp2((x - m_thread) * log2e) and rescaled
+    // by exp2((m_thread - m) * log2e), so the two agree up to the rounding of
+    // that per-thread rescale (a few fp32 ulp of the sum).  The one-FMA form
     // x*log2e - round(m*log2e) would scale every output by 2^(rounding error
     // of m*log2e), up to 2^(|m| * 2^-24), which the sum of pass 1 does not
     // share (0.15 % for a row at the fp16 lowest value).  x - m is exact near

@@ -4,8 +4,12 @@
 // models/qwen3/modeling_qwen3.py:81-82), run on flagos as silu
 // (csrc/aten/backends/cuda/silu.cu:15-35: x / (1 + exp(-x)) in fp32 opmath,
 // rounded to the tensor dtype) followed by mul (mul.cu:28-52).  The residual
-// add is add.Tensor (add.cu:48-84).  Pure streaming, launched as a full grid
-// (one 16-byte pack per thread; common.cuh full_grid).
+// add is add.Tensor (add.cu:48-84).  Pure streaming, launched as a full grid.
+// The hot kernel (swiglu32_kernel) runs 512-thread CTAs, each thread loading
+// two 32-byte packs (v8 accesses) of gate and up, one CTA per 1024 packs; the
+// residual rows, when present, are extra CTAs of the same launch.  Operands
+// not 32-byte aligned take the 16-byte kernels (one pack per thread, 256-thread
+// CTAs; common.cuh full_grid).
 #include "common.cuh"
 
 #include <algorithm>

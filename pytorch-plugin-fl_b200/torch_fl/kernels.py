@@ -237,11 +237,20 @@ def _broadcast(a: torch.Tensor, b: torch.Tensor):
     return shape, ea.stride(), eb.stride()
 
 
-def add(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0) -> torch.Tensor:
+def _binary_out(out, shape, a):
+    if out is None:
+        return torch.empty(shape, dtype=a.dtype, device=a.device)
+    if tuple(out.shape) != tuple(shape) or out.dtype != a.dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous tensor of the broadcast shape and dtype")
+    return out
+
+
+def add(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0,
+        out: torch.Tensor | None = None) -> torch.Tensor:
     if a.dtype != b.dtype:
         raise TypeError("add: operands must share a dtype (promote first)")
     shape, sa, sb = _broadcast(a, b)
-    out = torch.empty(shape, dtype=a.dtype, device=a.device)
+    out = _binary_out(out, shape, a)
     with _on_device(a):
         _abi.call("fl_b200_add", a.data_ptr(), _abi.i64_array(sa), b.data_ptr(),
                   _abi.i64_array(sb), out.data_ptr(), _abi.i64_array(shape), len(shape),
@@ -249,11 +258,11 @@ def add(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0) -> torch.Tensor:
     return out
 
 
-def mul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+def mul(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     if a.dtype != b.dtype:
         raise TypeError("mul: operands must share a dtype (promote first)")
     shape, sa, sb = _broadcast(a, b)
-    out = torch.empty(shape, dtype=a.dtype, device=a.device)
+    out = _binary_out(out, shape, a)
     with _on_device(a):
         _abi.call("fl_b200_mul", a.data_ptr(), _abi.i64_array(sa), b.data_ptr(),
                   _abi.i64_array(sb), out.data_ptr(), _abi.i64_array(shape), len(shape),

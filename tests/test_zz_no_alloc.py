@@ -58,6 +58,30 @@ def test_sum_all_noalloc_matches_workspace_entry(n, dtype):
         parity.assert_sum(np.float32(got), xn, None, f"noalloc call {call}")
 
 
+@pytest.mark.parametrize("n", [40_000_003, 777])
+def test_sum_all_noalloc_int32_to_int64_exact(n):
+    # The integer route of the same entry: int32 in, exact int64 out.
+    lib = _abi.load()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    g = torch.Generator(device=dev).manual_seed(99 + n)
+    x = torch.randint(-1000, 1001, (n,), generator=g, device=dev, dtype=torch.int32)
+    ws_bytes = lib.fl_b200_reduce_workspace_size(1, n)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    ref = torch.empty((), dtype=torch.int64, device=dev)
+    _abi.call("fl_b200_reduce_sum_all", x.data_ptr(), n, ref.data_ptr(), _abi.I32, _abi.I64,
+              ws.data_ptr(), ws_bytes, stream)
+    torch.cuda.synchronize(dev)
+    exact = int(x.cpu().numpy().astype(np.int64).sum())
+    assert ref.item() == exact
+    for call in range(2):
+        out = torch.full((), -1, dtype=torch.int64, device=dev)
+        _abi.call("fl_b200_reduce_sum_all_noalloc", x.data_ptr(), n, out.data_ptr(), _abi.I32,
+                  _abi.I64, stream)
+        torch.cuda.synchronize(dev)
+        assert out.item() == exact, (call, out.item(), exact)
+
+
 def test_sum_all_noalloc_rejects_bad_arguments():
     with pytest.raises(_abi.FlB200Error) as ei:
         _abi.call("fl_b200_reduce_sum_all_noalloc", None, -1, None, _abi.F32, _abi.F32, None)

@@ -418,6 +418,21 @@ def cpu_info():
     return model
 
 
+def capture_graph(fn):
+    """Capture `fn`'s launches as a CUDA graph (one warm-up run on a side
+    stream first, as torch.cuda.graph requires)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        fn()
+    torch.cuda.synchronize()
+    return gr
+
+
 def workload_config(args, world):
     """The workload both arms run (the same dict on the b200 and the
     reference line)."""
@@ -454,6 +469,8 @@ def main():
     ap.add_argument("--no-op-configs", action="store_true")
     ap.add_argument("--no-graph", action="store_true",
                     help="time the headline with eager launches instead of a CUDA graph replay")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="launch without programmatic dependent launch (the default uses it)")
     ap.add_argument("--profile-case", choices=sorted(PROFILE_CASES),
                     help="run one small case of one op once on GPU 0 and exit (for ncu)")
     args = ap.parse_args()
@@ -496,8 +513,11 @@ def main():
         return
 
     import torch_fl  # noqa: F401  (loads libfl_b200.so; fails loudly if missing)
+    from torch_fl import _abi
     from torch_fl import kernels as K
     from torch_fl import sharding
+
+    _abi.set_pdl(not args.no_pdl)
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -531,14 +551,7 @@ def main():
     # the same kernels on the same buffers without per-launch host work.
     graph = None
     if not args.no_graph:
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            stack.run(stack.x0)
-        torch.cuda.current_stream().wait_stream(side)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            stack.run(stack.x0)
+        graph = capture_graph(lambda: stack.run(stack.x0))
         for _ in range(args.warmup):
             graph.replay()
         barrier()
@@ -560,6 +573,30 @@ def main():
     ms = sharding.max_over_ranks(start.elapsed_time(end), dev)
     ms_per_step = ms / args.steps
     value = args.tokens * args.steps / (ms / 1e3)
+
+    # A/B of programmatic dependent launch: the same step captured with
+    # the opposite setting, timed the same way (every rank takes it).
+    pdl_ab = None
+    if graph is not None:
+        _abi.set_pdl(args.no_pdl)
+        g_ab = capture_graph(lambda: stack.run(stack.x0))
+        _abi.set_pdl(not args.no_pdl)
+        for _ in range(args.warmup):
+            g_ab.replay()
+        barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(args.steps):
+            g_ab.replay()
+        a1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ab_ms = sharding.max_over_ranks(a0.elapsed_time(a1), dev)
+        del g_ab
+        pdl_ab = {"pdl": args.no_pdl, "ms_per_step": ab_ms / args.steps,
+                  "value": args.tokens * args.steps / (ab_ms / 1e3),
+                  "what": "the same graph step captured with programmatic dependent launch "
+                          + ("on" if args.no_pdl else "off")}
 
     # Per-kernel durations: a second timed pass of the same steps launched
     # one by one with CUDA events around every launch (the events would add
@@ -730,10 +767,12 @@ def main():
             "config": workload_config(args, world),
             "impl_config": {"rounding": args.rounding,
                             "fused_add_rms_norm": not args.no_fuse_add_norm,
+                            "pdl": not args.no_pdl,
                             "launch": "CUDA graph replay of the step" if not args.no_graph
                                       else "eager launches"},
             "hbm_gbs_step": round(stack_bytes(stack) * args.steps / (ms / 1e3) / 1e9, 1),
             "per_op": per_op, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "pdl_ab": pdl_ab,
             "gpu_eager_reference": eager, "per_op_configs": per_op_configs,
             "gpu_launches": stack.launches_per_step() * args.steps,
             "per_kernel_pass_ms_per_step": round(timed_pass_ms, 3),
@@ -755,8 +794,13 @@ def op_configs(dev, peak, reps=5):
     out = {}
     g = torch.Generator(device=dev).manual_seed(7)
 
-    # written before every timed rep of a case whose inputs L2 could hold
+    # A case whose inputs L2 could hold gets an L2 flush before every timed
+    # rep: 256 MB written, then another 256 MB read, so that L2 holds clean
+    # lines of neither the case's inputs nor dirty flush data (whose
+    # write-back would otherwise land inside the timed kernel).
     flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_rd = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    flush_sink = torch.empty((), dtype=torch.float32, device=dev)
 
     def timed(name, fn, nbytes, note="", flush=False, tokens=None, reps_=None):
         for _ in range(2):
@@ -766,7 +810,8 @@ def op_configs(dev, peak, reps=5):
         for _ in range(reps_ or reps):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             if flush:
-                flush_buf.fill_(1)   # 256 MB > L2: the inputs come from HBM
+                flush_buf.fill_(1)
+                torch.sum(flush_rd, dim=0, out=flush_sink)
             # A bounded spin kernel keeps the GPU busy while the host prepares
             # the launch, so the events bracket the op's device time only.
             torch.cuda._sleep(2_000_000)
@@ -782,7 +827,7 @@ def op_configs(dev, peak, reps=5):
         if tokens:
             out[name]["tokens_per_s"] = round(tokens / (ms * 1e-3), 1)
         if flush:
-            out[name]["l2"] = "256 MB written before each rep"
+            out[name]["l2"] = "flushed before each rep (256 MB written, then 256 MB read)"
         if note:
             out[name]["note"] = note
 
@@ -921,31 +966,31 @@ def chain_configs(dev, g, timed, T=8192):
         rms(); rope()                 # noqa: E702
         K.swiglu_residual(gt, up, x, y, act_out=a, h_out=h)
 
-    def graph_of(fn):
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            fn()
-        torch.cuda.current_stream().wait_stream(side)
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr):
-            fn()
-        torch.cuda.synchronize()
-        return gr
-
     chain_bytes = (BYTES["rms_norm"] + BYTES["rope_qk"] + BYTES["swiglu"] + BYTES["residual_add"]
                    + TABLE_BYTES_PER_TOKEN) * T
     tag = f"llama_chain_T{T}"
-    g4, g3 = graph_of(chain4), graph_of(chain3)
+    from torch_fl import _abi
+
+    pdl = _abi.set_pdl(False)
+    g4n, g3n = capture_graph(chain4), capture_graph(chain3)
+    _abi.set_pdl(True)
+    g4, g3 = capture_graph(chain4), capture_graph(chain3)
+    _abi.set_pdl(pdl)
     timed(f"{tag}_graph", g4.replay, chain_bytes,
-          "RMSNorm, RoPE, SwiGLU, residual add: 4 b200 launches replayed as one CUDA graph",
-          flush=True, tokens=T, reps_=20)
+          "RMSNorm, RoPE, SwiGLU, residual add: 4 b200 launches replayed as one CUDA graph "
+          "(programmatic dependent launch)", flush=True, tokens=T, reps_=20)
+    timed(f"{tag}_graph_no_pdl", g4n.replay, chain_bytes,
+          "the same graph captured without programmatic dependent launch", flush=True,
+          tokens=T, reps_=20)
     timed(f"{tag}_eager", chain4, chain_bytes, "the same 4 launches, eager", flush=True,
           tokens=T, reps_=20)
     timed(f"{tag}_fused_graph", g3.replay, chain_bytes,
-          "RMSNorm, RoPE, SwiGLU+residual in one kernel: 3 launches as one CUDA graph",
-          flush=True, tokens=T, reps_=20)
-    del g4, g3
+          "RMSNorm, RoPE, SwiGLU+residual in one kernel: 3 launches as one CUDA graph "
+          "(programmatic dependent launch)", flush=True, tokens=T, reps_=20)
+    timed(f"{tag}_fused_graph_no_pdl", g3n.replay, chain_bytes,
+          "the same 3-launch graph without programmatic dependent launch", flush=True,
+          tokens=T, reps_=20)
+    del g4, g3, g4n, g3n
 
     def torch_chain():
         hf = x.to(torch.float32)
@@ -1016,6 +1061,9 @@ PROFILE_CASES = {
     "softmax_long": "softmax bf16 [512, 128256] (a vocabulary of logits per row)",
     "elementwise": "add bf16 [32768, 4096] + [32768, 4096]; mul by a [4096] row vector; "
                    "mul by a [32768, 1] column",
+    "chain_8192": "the 8192-token Llama chain: RMSNorm [8192, 4096], RoPE q [8192, 32, 128] / "
+                  "k [8192, 8, 128], SwiGLU [8192, 14336], residual add [8192, 4096]; then "
+                  "Qwen3 q/k-norm -> RoPE on the same q, k",
 }
 
 
@@ -1058,6 +1106,24 @@ def profile_case(name):
     elif name == "softmax_long":
         x = (3.0 * torch.randn(512, 128256, generator=g, device=dev)).to(torch.bfloat16)
         fn = lambda: K.softmax(x)  # noqa: E731
+    elif name == "chain_8192":
+        T = 8192
+
+        def rn(*shape, scale=1.0, loc=0.0):
+            return (loc + scale * torch.randn(*shape, generator=g, device=dev)).to(torch.bfloat16)
+
+        x, y, w = rn(T, HIDDEN), rn(T, HIDDEN), rn(HIDDEN, scale=0.1, loc=1.0)
+        q, k = rn(1, T, HQ, HEAD), rn(1, T, HKV, HEAD)
+        gt, up = rn(T, INTER), rn(T, INTER)
+        wq, wk = rn(HEAD, scale=0.1, loc=1.0), rn(HEAD, scale=0.1, loc=1.0)
+        cos, sin = rope_tables(0, T, dev)
+        n, h, a = torch.empty_like(x), torch.empty_like(x), torch.empty_like(gt)
+        qo, ko = torch.empty_like(q), torch.empty_like(k)
+        fn = lambda: (K.rms_norm(x, w, EPS, out=n),  # noqa: E731
+                      K.rope_qk(q, k, cos, sin, layout="bshd", q_out=qo, k_out=ko),
+                      K.swiglu(gt, up, out=a), K.add(x, y, out=h),
+                      K.rope_qk(q, k, cos, sin, layout="bshd", q_weight=wq, k_weight=wk,
+                                eps=1e-6, q_out=qo, k_out=ko))
     elif name == "masked_softmax":
         x = (3.0 * torch.randn(2, 32, 2048, 2048, generator=g, device=dev)).to(torch.bfloat16)
         m = torch.zeros(2, 1, 2048, 2048, dtype=torch.bfloat16, device=dev).masked_fill(

@@ -70,6 +70,14 @@ FL_B200_API int fl_b200_version(void);
 FL_B200_API const char* fl_b200_status_string(int status);
 /* Last CUDA error seen by a failed call on this thread (cudaError_t value). */
 FL_B200_API int fl_b200_last_cuda_error(void);
+/* Launch option, no counterpart in the reference (its cuda route launches    *
+ * PyTorch's kernels with <<<>>>).  With enable != 0 (the default; the        *
+ * environment variable FL_B200_PDL=0 turns it off at load) every kernel of   *
+ * this library is launched with programmatic stream serialization: it may    *
+ * begin while the previous kernel in the stream finishes, and waits on the   *
+ * device (griddepcontrol.wait) before its first memory access, so results    *
+ * are the same either way.  Process-wide; returns the previous setting.      */
+FL_B200_API int fl_b200_set_pdl(int enable);
 
 /* ------------------------------------------------------------------------ *
  * RMSNorm forward over the last dim:                                        *

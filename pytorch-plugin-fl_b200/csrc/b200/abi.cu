@@ -1,5 +1,6 @@
 // Library identity, status strings and the per-device geometry cache.
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -18,6 +19,16 @@ int launch_status() {
   }
   return FL_B200_OK;
 }
+
+namespace {
+int pdl_from_env() {
+  const char* v = std::getenv("FL_B200_PDL");
+  return (v != nullptr && v[0] == '0') ? 0 : 1;
+}
+std::atomic<int> g_pdl{pdl_from_env()};
+}  // namespace
+
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
 
 namespace {
 constexpr int kMaxDevices = 64;
@@ -72,5 +83,9 @@ FL_B200_API const char* fl_b200_status_string(int status) {
 }
 
 FL_B200_API int fl_b200_last_cuda_error(void) { return flb200::g_last_cuda_error; }
+
+FL_B200_API int fl_b200_set_pdl(int enable) {
+  return flb200::g_pdl.exchange(enable ? 1 : 0, std::memory_order_relaxed);
+}
 
 }  // extern "C"

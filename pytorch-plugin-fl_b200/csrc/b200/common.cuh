@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <type_traits>
+#include <utility>
 
 #include "../../../include/fl_b200.h"
 
@@ -388,6 +389,45 @@ int blocks_per_sm(K kernel, int block, size_t smem) {
     n = 1;
   }
   return n;
+}
+
+// ------------------------------------------- programmatic dependent launch --
+// Kernels of this library may be launched with programmatic stream
+// serialization (PDL): such a launch can begin while the previous kernel in
+// the stream is still running, as soon as every CTA of that kernel has
+// started.  Its CTAs then become resident as the previous kernel's CTAs
+// retire and wait in griddepcontrol.wait, which returns once the previous
+// grid has completed and its memory operations are visible; so a kernel's
+// launch latency and CTA rasterisation overlap the previous kernel's tail.
+// Every kernel calls pdl_prologue() before its first global memory access
+// (read or write), which makes the overlap safe for any producer/consumer
+// order.  Launched without the attribute, both instructions return at once.
+__device__ __forceinline__ void pdl_prologue() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Dependents may launch as soon as every CTA of this grid has passed here.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// True when launches use programmatic stream serialization (fl_b200_set_pdl;
+// FL_B200_PDL=0 in the environment turns it off at load).
+bool pdl_enabled();
+
+// Launches `kern` on `stream`, with programmatic stream serialization when
+// pdl_enabled().  A launch error is left for launch_status() to report.
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  (void)cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // One CTA per work unit ("full grid").  Measured on B200 for every streaming

@@ -39,6 +39,7 @@ __device__ __forceinline__ I apply_i(I a, I b, I alpha) {
 template <typename T, int OP>
 __global__ void __launch_bounds__(kBlock)
 binary_dense_kernel(const T* a, const T* b, T* o, int64_t npk, float alpha) {
+  pdl_prologue();
   constexpr int VW = Elem<T>::kVec;
   const int64_t nth = (int64_t)gridDim.x * kBlock;
   int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x;
@@ -80,6 +81,7 @@ constexpr int kPacks32 = 2;
 template <typename T, int OP>
 __global__ void __launch_bounds__(kBlock32)
 binary_dense32_kernel(const T* a, const T* b, T* o, int64_t npk32, float alpha) {
+  pdl_prologue();
   constexpr int VW = Elem<T>::kVec;
   const int64_t i0 = (int64_t)blockIdx.x * (kBlock32 * kPacks32) + threadIdx.x;
   Pack32 av[kPacks32], bv[kPacks32];
@@ -129,6 +131,7 @@ template <typename T, int OP, int MODE, bool VEC_FIRST>
 __global__ void __launch_bounds__(kBlock)
 binary_bcast_rows_kernel(const T* full, const T* vec, int64_t s_stride, T* o, int64_t rows,
                          int64_t cpk, float alpha) {
+  pdl_prologue();
   constexpr int VW = Elem<T>::kVec;
   const int64_t r0 = (int64_t)blockIdx.x * kTileRows;
   float sv[kTileRows];
@@ -185,6 +188,7 @@ __device__ __forceinline__ void nd_offsets(const NdArgs& g, int64_t i, int64_t& 
 template <typename T, int OP>
 __global__ void __launch_bounds__(kBlock)
 binary_nd_float_kernel(const T* a, const T* b, T* o, int64_t n, NdArgs g, float alpha) {
+  pdl_prologue();
   for (int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * kBlock) {
     int64_t oa, ob;
@@ -196,6 +200,7 @@ binary_nd_float_kernel(const T* a, const T* b, T* o, int64_t n, NdArgs g, float 
 template <typename I, int OP>
 __global__ void __launch_bounds__(kBlock)
 binary_nd_int_kernel(const I* a, const I* b, I* o, int64_t n, NdArgs g, I alpha) {
+  pdl_prologue();
   for (int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * kBlock) {
     int64_t oa, ob;
@@ -208,6 +213,7 @@ binary_nd_int_kernel(const I* a, const I* b, I* o, int64_t n, NdArgs g, I alpha)
 template <typename T, int OP>
 __global__ void __launch_bounds__(kBlock)
 scalar_float_kernel(const T* a, T* o, int64_t n, float s, float alpha) {
+  pdl_prologue();
   for (int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * kBlock)
     o[i] = Elem<T>::from_f(apply_f<OP>(Elem<T>::to_f(a[i]), s, alpha));
@@ -215,6 +221,7 @@ scalar_float_kernel(const T* a, T* o, int64_t n, float s, float alpha) {
 template <typename T, int OP>
 __global__ void __launch_bounds__(kBlock)
 scalar_float_vec_kernel(const T* a, T* o, int64_t npk, float s, float alpha) {
+  pdl_prologue();
   constexpr int VW = Elem<T>::kVec;
   for (int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x; i < npk;
        i += (int64_t)gridDim.x * kBlock) {
@@ -230,6 +237,7 @@ scalar_float_vec_kernel(const T* a, T* o, int64_t npk, float s, float alpha) {
 template <typename T, int OP>
 __global__ void __launch_bounds__(kBlock32)
 scalar_float_vec32_kernel(const T* a, T* o, int64_t npk32, float s, float alpha) {
+  pdl_prologue();
   constexpr int VW = Elem<T>::kVec;
   const int64_t i0 = (int64_t)blockIdx.x * (kBlock32 * kPacks32) + threadIdx.x;
   Pack32 av[kPacks32];
@@ -258,6 +266,7 @@ scalar_float_vec32_kernel(const T* a, T* o, int64_t npk32, float s, float alpha)
 template <typename I, int OP>
 __global__ void __launch_bounds__(kBlock)
 scalar_int_kernel(const I* a, I* o, int64_t n, I s, I alpha) {
+  pdl_prologue();
   for (int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * kBlock)
     o[i] = apply_i<OP, I>(a[i], s, alpha);
@@ -298,6 +307,7 @@ __device__ __forceinline__ D convert(S v) {
 
 template <typename S, typename D>
 __global__ void __launch_bounds__(kBlock) cast_kernel(const S* src, D* dst, int64_t n) {
+  pdl_prologue();
   const int64_t nth = (int64_t)gridDim.x * kBlock;
   int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x;
   // 4 independent elements per iteration for memory-level parallelism.
@@ -318,6 +328,7 @@ __global__ void __launch_bounds__(kBlock) cast_kernel(const S* src, D* dst, int6
 template <typename S, typename D>
 __global__ void __launch_bounds__(kBlock)
 cast_vec8_kernel(const S* src, D* dst, int64_t n8) {
+  pdl_prologue();
   for (int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x; i < n8;
        i += (int64_t)gridDim.x * kBlock) {
     union {
@@ -430,8 +441,8 @@ int binary_entry(const void* a, const int64_t* sa, const void* b, const int64_t*
     T* op = static_cast<T*>(out);
     if constexpr (std::is_integral<T>::value) {
       auto kern = binary_nd_int_kernel<T, OP>;
-      kern<<<grid_for(kern, n, dev, 4), kBlock, 0, stream>>>(ap, bp, op, n, g,
-                                                             (T)(int64_t)alpha);
+      launch_k(kern, grid_for(kern, n, dev, 4), kBlock, 0, stream, ap, bp, op, n, g,
+               (T)(int64_t)alpha);
       return launch_status();
     } else {
       constexpr int VW = Elem<T>::kVec;
@@ -442,16 +453,16 @@ int binary_entry(const void* a, const int64_t* sa, const void* b, const int64_t*
       if (a_dense && b_dense && n % (2 * VW) == 0 && aligned32(ap) && aligned32(bp) &&
           aligned32(op)) {
         const int64_t npk32 = n / (2 * VW);
-        binary_dense32_kernel<T, OP>
-            <<<full_grid(ceil_div(npk32, (int64_t)kBlock32 * kPacks32)), kBlock32, 0, stream>>>(
-                ap, bp, op, npk32, al);
+        launch_k((binary_dense32_kernel<T, OP>),
+                 full_grid(ceil_div(npk32, (int64_t)kBlock32 * kPacks32)), kBlock32, 0,
+                 stream, ap, bp, op, npk32, al);
         return launch_status();
       }
       if (a_dense && b_dense && n % VW == 0 && all_aligned) {
         auto kern = binary_dense_kernel<T, OP>;
         const int64_t npk = n / VW;
         const int grid = full_grid(ceil_div(npk, kBlock));
-        kern<<<grid, kBlock, 0, stream>>>(ap, bp, op, npk, al);
+        launch_k(kern, grid, kBlock, 0, stream, ap, bp, op, npk, al);
         return launch_status();
       }
       const int64_t cols = ndim ? sz[ndim - 1] : 1;
@@ -461,29 +472,29 @@ int binary_entry(const void* a, const int64_t* sa, const void* b, const int64_t*
         int64_t rs = 0;
         // full op v[c] / v[c] op full (v 16-byte aligned)
         if (a_dense && aligned16(ap) && aligned16(bp) && rowvec_strides(sz, sb_, ndim)) {
-          binary_bcast_rows_kernel<T, OP, kRowVec, false>
-              <<<grid, kBlock, 0, stream>>>(ap, bp, 0, op, rows, cpk, al);
+          launch_k((binary_bcast_rows_kernel<T, OP, kRowVec, false>), grid, kBlock, 0, stream,
+                   ap, bp, 0, op, rows, cpk, al);
           return launch_status();
         }
         if (b_dense && aligned16(ap) && aligned16(bp) && rowvec_strides(sz, sa_, ndim)) {
-          binary_bcast_rows_kernel<T, OP, kRowVec, true>
-              <<<grid, kBlock, 0, stream>>>(bp, ap, 0, op, rows, cpk, al);
+          launch_k((binary_bcast_rows_kernel<T, OP, kRowVec, true>), grid, kBlock, 0, stream,
+                   bp, ap, 0, op, rows, cpk, al);
           return launch_status();
         }
         // full op s[r] / s[r] op full (one value per row, any alignment)
         if (a_dense && aligned16(ap) && colvec_strides(sz, sb_, ndim, &rs)) {
-          binary_bcast_rows_kernel<T, OP, kColVec, false>
-              <<<grid, kBlock, 0, stream>>>(ap, bp, rs, op, rows, cpk, al);
+          launch_k((binary_bcast_rows_kernel<T, OP, kColVec, false>), grid, kBlock, 0, stream,
+                   ap, bp, rs, op, rows, cpk, al);
           return launch_status();
         }
         if (b_dense && aligned16(bp) && colvec_strides(sz, sa_, ndim, &rs)) {
-          binary_bcast_rows_kernel<T, OP, kColVec, true>
-              <<<grid, kBlock, 0, stream>>>(bp, ap, rs, op, rows, cpk, al);
+          launch_k((binary_bcast_rows_kernel<T, OP, kColVec, true>), grid, kBlock, 0, stream,
+                   bp, ap, rs, op, rows, cpk, al);
           return launch_status();
         }
       }
       auto kern = binary_nd_float_kernel<T, OP>;
-      kern<<<grid_for(kern, n, dev, 4), kBlock, 0, stream>>>(ap, bp, op, n, g, al);
+      launch_k(kern, grid_for(kern, n, dev, 4), kBlock, 0, stream, ap, bp, op, n, g, al);
       return launch_status();
     }
   });
@@ -497,10 +508,10 @@ int cast_from(const S* src, void* dst, int dst_dtype, int64_t n, const DeviceInf
     D* dp = static_cast<D*>(dst);
     if (n % 8 == 0 && aligned16(src) && aligned16(dp)) {
       auto kern = cast_vec8_kernel<S, D>;
-      kern<<<grid_for(kern, n / 8, dev), kBlock, 0, stream>>>(src, dp, n / 8);
+      launch_k(kern, grid_for(kern, n / 8, dev), kBlock, 0, stream, src, dp, n / 8);
     } else {
       auto kern = cast_kernel<S, D>;
-      kern<<<grid_for(kern, ceil_div(n, 4), dev), kBlock, 0, stream>>>(src, dp, n);
+      launch_k(kern, grid_for(kern, ceil_div(n, 4), dev), kBlock, 0, stream, src, dp, n);
     }
     return launch_status();
   });
@@ -545,23 +556,23 @@ FL_B200_API int fl_b200_binary_scalar(const void* a, double s, void* out, int64_
       constexpr int OP = decltype(opc)::value;
       if constexpr (std::is_integral<T>::value) {
         auto kern = scalar_int_kernel<T, OP>;
-        kern<<<grid_for(kern, n, dev, 4), kBlock, 0, cs>>>(ap, outp, n, (T)(int64_t)s,
-                                                           (T)(int64_t)alpha);
+        launch_k(kern, grid_for(kern, n, dev, 4), kBlock, 0, cs, ap, outp, n, (T)(int64_t)s,
+                 (T)(int64_t)alpha);
       } else {
         constexpr int VW = Elem<T>::kVec;
         if (n % (2 * VW) == 0 && aligned32(ap) && aligned32(outp)) {
           const int64_t npk32 = n / (2 * VW);
-          scalar_float_vec32_kernel<T, OP>
-              <<<full_grid(ceil_div(npk32, (int64_t)kBlock32 * kPacks32)), kBlock32, 0, cs>>>(
-                  ap, outp, npk32, (float)s, (float)alpha);
+          launch_k((scalar_float_vec32_kernel<T, OP>),
+                   full_grid(ceil_div(npk32, (int64_t)kBlock32 * kPacks32)), kBlock32, 0, cs,
+                   ap, outp, npk32, (float)s, (float)alpha);
         } else if (n % VW == 0 && aligned16(ap) && aligned16(outp)) {
           auto kern = scalar_float_vec_kernel<T, OP>;
-          kern<<<grid_for(kern, n / VW, dev), kBlock, 0, cs>>>(ap, outp, n / VW, (float)s,
-                                                               (float)alpha);
+          launch_k(kern, grid_for(kern, n / VW, dev), kBlock, 0, cs, ap, outp, n / VW,
+                   (float)s, (float)alpha);
         } else {
           auto kern = scalar_float_kernel<T, OP>;
-          kern<<<grid_for(kern, n, dev, 4), kBlock, 0, cs>>>(ap, outp, n, (float)s,
-                                                             (float)alpha);
+          launch_k(kern, grid_for(kern, n, dev, 4), kBlock, 0, cs, ap, outp, n, (float)s,
+                   (float)alpha);
         }
       }
       return launch_status();

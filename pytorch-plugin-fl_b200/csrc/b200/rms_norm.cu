@@ -39,6 +39,7 @@ template <typename T, int TPR, int VPT, int BLOCK, bool CHAIN, bool ADD>
 __global__ void __launch_bounds__(BLOCK, ladder_min_blocks<BLOCK>())
 rms_norm_vec_kernel(const T* x, int64_t ldx, const T* y, T* h, const T* w, T* out,
                     int64_t ldo, int64_t rows, int nvec, float eps, float cols_f) {
+  pdl_prologue();
   constexpr int VW = Elem<T>::kVec;
   constexpr int RPB = BLOCK / TPR;
   __shared__ float smem[BLOCK / 32];
@@ -135,6 +136,7 @@ __global__ void __launch_bounds__(BLOCK, ladder_min_blocks<BLOCK>())
 add_rms_norm_w32_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict__ y,
                         T* __restrict__ h, const T* __restrict__ w, T* __restrict__ out,
                         int64_t ldo, int64_t rows, int nvec32, float eps, float cols_f) {
+  pdl_prologue();
   constexpr int VW = Elem<T>::kVec;
   constexpr int E = 2 * VW;  // elements per 32-byte pack
   constexpr int NP = E / 2;  // fp32 pairs per 32-byte pack
@@ -225,6 +227,7 @@ template <typename T, bool CHAIN, bool ADD>
 __global__ void __launch_bounds__(256)
 rms_norm_loop_kernel(const T* x, int64_t ldx, const T* y, T* h, const T* w, T* out,
                      int64_t ldo, int64_t rows, int64_t cols, float eps) {
+  pdl_prologue();
   __shared__ float smem[256 / 32];
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const T* xr = x + row * ldx;
@@ -267,9 +270,9 @@ int launch_rms_norm(const T* x, int64_t ldx, const T* y, T* h, const T* w, T* ou
         constexpr int TPR = decltype(tpr)::value;
         constexpr int VPT = decltype(vpt)::value;
         constexpr int BLOCK = ladder_block<TPR>();
-        add_rms_norm_w32_kernel<T, TPR, VPT, BLOCK, CHAIN>
-            <<<full_grid(ceil_div(rows, BLOCK / TPR)), BLOCK, 0, stream>>>(
-                x, ldx, y, h, w, out, ldo, rows, (int)(cols / E), eps, (float)cols);
+        launch_k((add_rms_norm_w32_kernel<T, TPR, VPT, BLOCK, CHAIN>),
+                 full_grid(ceil_div(rows, BLOCK / TPR)), BLOCK, 0, stream, x, ldx, y, h, w,
+                 out, ldo, rows, (int)(cols / E), eps, (float)cols);
         return launch_status();
       };
       // one 32-byte pack per thread from 129 to 1024 packs (4096-wide bf16
@@ -296,8 +299,8 @@ int launch_rms_norm(const T* x, int64_t ldx, const T* y, T* h, const T* w, T* ou
       auto kern = rms_norm_vec_kernel<T, TPR, VPT, BLOCK, CHAIN, ADD>;
       const int64_t units = ceil_div(rows, BLOCK / TPR);
       const int grid = full_grid(units);
-      kern<<<grid, BLOCK, 0, stream>>>(x, ldx, y, h, w, out, ldo, rows, (int)nvec, eps,
-                                       (float)cols);
+      launch_k(kern, grid, BLOCK, 0, stream, x, ldx, y, h, w, out, ldo, rows, (int)nvec, eps,
+               (float)cols);
       return launch_status();
     });
     if (r >= 0) return r;
@@ -305,7 +308,7 @@ int launch_rms_norm(const T* x, int64_t ldx, const T* y, T* h, const T* w, T* ou
   auto kern = rms_norm_loop_kernel<T, CHAIN, ADD>;
   static const int per_sm = blocks_per_sm(kern, 256, 0);
   const int grid = (int)std::min<int64_t>(rows, (int64_t)per_sm * dev.sm_count);
-  kern<<<grid, 256, 0, stream>>>(x, ldx, y, h, w, out, ldo, rows, cols, eps);
+  launch_k(kern, grid, 256, 0, stream, x, ldx, y, h, w, out, ldo, rows, cols, eps);
   return launch_status();
 }
 

@@ -48,6 +48,7 @@ __device__ __forceinline__ void rope_pair(float xl, float xh, float cl, float sl
 
 template <typename T, int G, bool NORM, bool CHAIN>
 __global__ void __launch_bounds__(256) rope_vec_kernel(RopeArgs a, uint32_t units) {
+  pdl_prologue();
   constexpr int VW = Elem<T>::kVec;
   constexpr int UPB = 256 / G;  // head rows per CTA iteration
   const int j = threadIdx.x % G;
@@ -132,6 +133,7 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(RopeArgs a, uint32_t unit
 // per-row index division, table loads amortised over all heads of the token.
 template <typename T, int G, bool NORM, bool CHAIN, int U>
 __global__ void __launch_bounds__(256) rope_token_kernel(RopeArgs a, uint32_t tokens) {
+  pdl_prologue();
   constexpr int VW = Elem<T>::kVec;
   constexpr int SLOTS = 32 / G;
   const int lane = threadIdx.x & 31;
@@ -141,6 +143,20 @@ __global__ void __launch_bounds__(256) rope_token_kernel(RopeArgs a, uint32_t to
   const uint32_t half = a.D / 2;
   const uint32_t dl = j * VW;
   const uint32_t warps = blockDim.x / 32;
+  // The norm weights are the same for every token: each lane keeps its packs
+  // of both halves of w_q and w_k as loaded (16-bit encodings for bf16/f16),
+  // so a head step needs no weight load.
+  uint4 wql = make_uint4(0, 0, 0, 0), wqh = wql, wkl = wql, wkh = wql;
+  if constexpr (NORM) {
+    if (a.Hq > 0) {
+      wql = ld_cached(static_cast<const T*>(a.wq) + dl);
+      wqh = ld_cached(static_cast<const T*>(a.wq) + half + dl);
+    }
+    if (a.Hk > 0) {
+      wkl = ld_cached(static_cast<const T*>(a.wk) + dl);
+      wkh = ld_cached(static_cast<const T*>(a.wk) + half + dl);
+    }
+  }
   for (uint32_t token = blockIdx.x * warps + threadIdx.x / 32; token < tokens;
        token += gridDim.x * warps) {  // warp-uniform
     const uint32_t b = token / a.S;
@@ -168,23 +184,21 @@ __global__ void __launch_bounds__(256) rope_token_kernel(RopeArgs a, uint32_t to
     for (uint32_t h0 = 0; h0 < htot; h0 += SLOTS * U) {  // warp-uniform
       uint4 lo[U], hi[U];
       T* dst[U];
-      const T* w[U];
-      bool valid[U];
+      bool valid[U], isq_[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const uint32_t h = h0 + u * SLOTS + slot;
         valid[u] = h < htot;
         const bool isq = h < a.Hq;
+        isq_[u] = isq;
         const uint32_t hh = isq ? h : h - a.Hq;
         const T* src;
         if (isq) {
           src = static_cast<const T*>(a.q) + b * a.sq[0] + hh * a.sq[1] + s * a.sq[2];
           dst[u] = static_cast<T*>(a.qo) + b * a.soq[0] + hh * a.soq[1] + s * a.soq[2];
-          w[u] = static_cast<const T*>(a.wq);
         } else {
           src = static_cast<const T*>(a.k) + b * a.sk[0] + hh * a.sk[1] + s * a.sk[2];
           dst[u] = static_cast<T*>(a.ko) + b * a.sok[0] + hh * a.sok[1] + s * a.sok[2];
-          w[u] = static_cast<const T*>(a.wk);
         }
         lo[u] = make_uint4(0, 0, 0, 0);
         hi[u] = make_uint4(0, 0, 0, 0);
@@ -206,8 +220,8 @@ __global__ void __launch_bounds__(256) rope_token_kernel(RopeArgs a, uint32_t to
           const float r = 1.0f / sqrtf(ss / (float)a.D + a.eps);
           if (valid[u]) {
             float wl[VW], wh[VW];
-            unpack<T>(ld_cached(w[u] + dl), wl);
-            unpack<T>(ld_cached(w[u] + half + dl), wh);
+            unpack<T>(isq_[u] ? wql : wkl, wl);
+            unpack<T>(isq_[u] ? wqh : wkh, wh);
 #pragma unroll
             for (int e = 0; e < VW; ++e) {
               if (CHAIN) {
@@ -249,6 +263,7 @@ __global__ void __launch_bounds__(256) rope_token_kernel(RopeArgs a, uint32_t to
 // Any alignment / head dim: one warp per head row, scalar element access.
 template <typename T, bool NORM, bool CHAIN>
 __global__ void __launch_bounds__(256) rope_scalar_kernel(RopeArgs a, uint32_t units) {
+  pdl_prologue();
   constexpr int UPB = 256 / 32;
   const int lane = threadIdx.x & 31;
   const uint32_t htot = a.Hq + a.Hk;
@@ -317,7 +332,7 @@ int launch_vec(const RopeArgs& a, uint32_t units, const DeviceInfo& dev,
   static const int per_sm = blocks_per_sm(kern, 256, 0);
   const int64_t blocks = ceil_div(units, 256 / G);
   const int grid = (int)std::min<int64_t>(blocks, (int64_t)per_sm * dev.sm_count);
-  kern<<<grid, 256, 0, stream>>>(a, units);
+  launch_k(kern, grid, 256, 0, stream, a, units);
   return launch_status();
 }
 
@@ -330,9 +345,9 @@ int launch_token(const RopeArgs& a, uint32_t tokens, cudaStream_t stream) {
   const uint32_t steps = (a.Hq + a.Hk + kSlots - 1) / kSlots;  // head steps per token
   const int grid = full_grid(ceil_div(tokens, 8));
   if (steps % 5 == 0) {
-    rope_token_kernel<T, G, NORM, CHAIN, 5><<<grid, 256, 0, stream>>>(a, tokens);
+    launch_k((rope_token_kernel<T, G, NORM, CHAIN, 5>), grid, 256, 0, stream, a, tokens);
   } else {
-    rope_token_kernel<T, G, NORM, CHAIN, 4><<<grid, 256, 0, stream>>>(a, tokens);
+    launch_k((rope_token_kernel<T, G, NORM, CHAIN, 4>), grid, 256, 0, stream, a, tokens);
   }
   return launch_status();
 }
@@ -370,7 +385,7 @@ int launch_rope(const RopeArgs& a, uint32_t units, cudaStream_t stream) {
   static const int per_sm = blocks_per_sm(kern, 256, 0);
   const int64_t blocks = ceil_div(units, 8);
   const int grid = (int)std::min<int64_t>(blocks, (int64_t)per_sm * dev.sm_count);
-  kern<<<grid, 256, 0, stream>>>(a, units);
+  launch_k(kern, grid, 256, 0, stream, a, units);
   return launch_status();
 }
 

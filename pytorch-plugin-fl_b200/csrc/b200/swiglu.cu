@@ -97,6 +97,7 @@ __device__ __forceinline__ void add_dense(const T* x, const T* y, T* h, int64_t 
 template <typename T, bool CHAIN>
 __global__ void __launch_bounds__(kBlock)
 swiglu_vec_kernel(const T* g, const T* u, T* o, int64_t n) {
+  pdl_prologue();
   swiglu_dense<T, CHAIN>(g, u, o, n, (int64_t)blockIdx.x * kBlock + threadIdx.x,
                          (int64_t)gridDim.x * kBlock);
 }
@@ -107,6 +108,7 @@ template <typename T, bool CHAIN>
 __global__ void __launch_bounds__(kBlock)
 swiglu_residual_kernel(const T* g, const T* u, T* act, int64_t n_act, const T* x,
                        const T* y, T* h, int64_t n_res) {
+  pdl_prologue();
   const int64_t tid = (int64_t)blockIdx.x * kBlock + threadIdx.x;
   const int64_t nth = (int64_t)gridDim.x * kBlock;
   swiglu_dense<T, CHAIN>(g, u, act, n_act, tid, nth);
@@ -126,6 +128,7 @@ template <typename T, bool CHAIN>
 __global__ void __launch_bounds__(kBlock32)
 swiglu32_kernel(const T* g, const T* u, T* act, int64_t n_act, int64_t act_blocks,
                 const T* x, const T* y, T* h, int64_t n_res) {
+  pdl_prologue();
   constexpr int VW2 = 2 * Elem<T>::kVec;  // elements per 32-byte pack
   const bool is_act = (int64_t)blockIdx.x < act_blocks;
   const int64_t blk = is_act ? (int64_t)blockIdx.x : (int64_t)blockIdx.x - act_blocks;
@@ -167,8 +170,8 @@ int launch_swiglu32(const T* g, const T* u, T* act, int64_t n_act, const T* x, c
   constexpr int64_t kChunk = (int64_t)kBlock32 * kPacks32;
   const int64_t ba = ceil_div(pa, kChunk), br = ceil_div(pr, kChunk);
   if (ba + br > 0x7fffffff) return FL_B200_ERR_TOO_LARGE;
-  swiglu32_kernel<T, CHAIN><<<(int)std::max<int64_t>(ba + br, 1), kBlock32, 0, stream>>>(
-      g, u, act, pa, ba, x, y, h, pr);
+  launch_k((swiglu32_kernel<T, CHAIN>), (int)std::max<int64_t>(ba + br, 1), kBlock32, 0,
+           stream, g, u, act, pa, ba, x, y, h, pr);
   return launch_status();
 }
 
@@ -177,6 +180,7 @@ template <typename T, bool CHAIN>
 __global__ void __launch_bounds__(kBlock)
 swiglu_strided_kernel(const T* g, int64_t ldg, const T* u, int64_t ldu, T* o,
                       int64_t ldo, int64_t rows, int64_t cols) {
+  pdl_prologue();
   const int64_t n = rows * cols;
   for (int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * kBlock) {
@@ -202,12 +206,12 @@ int launch_swiglu(const T* g, int64_t ldg, const T* u, int64_t ldu, T* o, int64_
     auto kern = swiglu_vec_kernel<T, CHAIN>;
     const int64_t npk = n / VW;
     const int grid = full_grid(ceil_div(npk, kBlock));  // one pack per thread
-    kern<<<grid, kBlock, 0, stream>>>(g, u, o, npk);
+    launch_k(kern, grid, kBlock, 0, stream, g, u, o, npk);
     return launch_status();
   }
   auto kern = swiglu_strided_kernel<T, CHAIN>;
   const int grid = full_grid(ceil_div(n, kBlock));
-  kern<<<grid, kBlock, 0, stream>>>(g, ldg, u, ldu, o, ldo, rows, cols);
+  launch_k(kern, grid, kBlock, 0, stream, g, ldg, u, ldu, o, ldo, rows, cols);
   return launch_status();
 }
 
@@ -229,7 +233,7 @@ int launch_swiglu_residual(const T* g, const T* u, T* act, int64_t inter, const 
   auto kern = swiglu_residual_kernel<T, CHAIN>;
   const int64_t npk = std::max(n1, n2) / VW;
   const int grid = full_grid(ceil_div(npk, kBlock));  // one pack of each part per thread
-  kern<<<grid, kBlock, 0, stream>>>(g, u, act, n1 / VW, x, y, h, n2 / VW);
+  launch_k(kern, grid, kBlock, 0, stream, g, u, act, n1 / VW, x, y, h, n2 / VW);
   return launch_status();
 }
 

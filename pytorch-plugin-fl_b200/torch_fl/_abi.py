@@ -31,6 +31,7 @@ PROTOTYPES: dict[str, tuple] = {
     "fl_b200_version": (_i32, []),
     "fl_b200_status_string": (C.c_char_p, [_i32]),
     "fl_b200_last_cuda_error": (_i32, []),
+    "fl_b200_set_pdl": (_i32, [_i32]),
     "fl_b200_rms_norm_fwd": (
         _i32, [_p, _i64, _p, _p, _i64, _i64, _i64, _f32, _i32, _i32, _p]),
     "fl_b200_add_rms_norm_fwd": (
@@ -127,6 +128,13 @@ def call(name: str, *args) -> None:
     st = getattr(lib_, name)(*args)
     if st != 0:
         raise FlB200Error(name, st, lib_.fl_b200_last_cuda_error())
+
+
+def set_pdl(enable: bool) -> bool:
+    """Launch the library's kernels with programmatic dependent launch (the
+    default) or without; returns the previous setting.  Results are the
+    same either way."""
+    return bool(load().fl_b200_set_pdl(1 if enable else 0))
 
 
 def i64_array(vals) -> C.Array:

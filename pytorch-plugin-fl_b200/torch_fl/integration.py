@@ -10,10 +10,16 @@ modules, the module-level `apply_rotary_pos_emb`, the SwiGLU MLP forward and
 the module-level `eager_attention_forward` (its scale + mask + softmax +
 cast tail becomes one flagos::masked_softmax launch; the two matmuls stay
 torch's) of the Qwen3 / Qwen2 / Llama / Mistral model files with the
-flagos:: fused kernels.  The hooks act on device tensors (flagos or cuda), in inference and
-in training (the fused ops carry autograd formulas, torch_fl/autograd.py);
-CPU tensors, RoPE tables that themselves need a gradient, and attention
-with dropout active, run the original HF code unchanged.  `disable_hf_fused_ops()` restores the originals.
+flagos:: fused kernels.  Two forwards are replaced so that neighbouring ops
+run as one kernel: the decoder layer's (the residual add after attention and
+`post_attention_layernorm` become one flagos::add_rms_norm), and Qwen3's
+attention (`q_norm` / `k_norm` and `apply_rotary_pos_emb` become one
+flagos::rms_norm_rope; the projections, the KV cache update and the
+attention interface are HF's own).  The hooks act on device tensors (flagos
+or cuda), in inference and in training (the fused ops carry autograd
+formulas, torch_fl/autograd.py); CPU tensors, RoPE tables that themselves
+need a gradient, and attention with dropout active, run the original HF code
+unchanged.  `disable_hf_fused_ops()` restores the originals.
 """
 
 from __future__ import annotations
@@ -47,10 +53,11 @@ def get_registered_ops() -> list:
 
 # ------------------------------------------------------------- HF fused hooks
 _MODEL_FILES = {
-    "qwen3": ("Qwen3RMSNorm", "Qwen3MLP"),
-    "qwen2": ("Qwen2RMSNorm", "Qwen2MLP"),
-    "llama": ("LlamaRMSNorm", "LlamaMLP"),
-    "mistral": ("MistralRMSNorm", "MistralMLP"),
+    # RMSNorm, MLP, decoder layer, attention with q/k norms (Qwen3 only)
+    "qwen3": ("Qwen3RMSNorm", "Qwen3MLP", "Qwen3DecoderLayer", "Qwen3Attention"),
+    "qwen2": ("Qwen2RMSNorm", "Qwen2MLP", "Qwen2DecoderLayer", None),
+    "llama": ("LlamaRMSNorm", "LlamaMLP", "LlamaDecoderLayer", None),
+    "mistral": ("MistralRMSNorm", "MistralMLP", "MistralDecoderLayer", None),
 }
 _saved: dict = {}
 _rounding: Optional[str] = None
@@ -126,6 +133,92 @@ def _attention_fn(orig):
     return eager_attention_forward
 
 
+def _norm_weight(norm, like: torch.Tensor):
+    """The weight of an HF RMSNorm module when the b200 kernel can take it,
+    else None (another norm class, or a weight of another dtype/device)."""
+    w = getattr(norm, "weight", None)
+    eps = getattr(norm, "variance_epsilon", None)
+    if (eps is None or not isinstance(w, torch.Tensor) or w.dim() != 1
+            or w.dtype != like.dtype or not _fusable(w, like)):
+        return None
+    return w
+
+
+def _decoder_forward(orig):
+    """The decoder layer of Qwen3 / Qwen2 / Llama / Mistral (one forward in
+    all four files: residual -> input_layernorm -> self_attn -> residual add
+    -> post_attention_layernorm -> mlp -> residual add) with the residual add
+    after attention and post_attention_layernorm as one add_rms_norm."""
+
+    def forward(self, hidden_states, attention_mask=None, position_ids=None,
+                past_key_values=None, use_cache=False, position_embeddings=None, **kwargs):
+        post = self.post_attention_layernorm
+        w = _norm_weight(post, hidden_states)
+        if w is None or hidden_states.shape[-1] != w.shape[0]:
+            return orig(self, hidden_states, attention_mask=attention_mask,
+                        position_ids=position_ids, past_key_values=past_key_values,
+                        use_cache=use_cache, position_embeddings=position_embeddings, **kwargs)
+        residual = hidden_states
+        hidden_states = self.input_layernorm(hidden_states)
+        hidden_states, _ = self.self_attn(
+            hidden_states=hidden_states, attention_mask=attention_mask,
+            position_ids=position_ids, past_key_values=past_key_values, use_cache=use_cache,
+            position_embeddings=position_embeddings, **kwargs)
+        if hidden_states.dtype == residual.dtype and hidden_states.shape == residual.shape:
+            # (residual + attn) and its norm in one pass; x + y == y + x bit for bit
+            normed, hidden_states = ops.add_rms_norm(hidden_states, residual, w,
+                                                     post.variance_epsilon, _rounding)
+        else:
+            hidden_states = residual + hidden_states
+            normed = post(hidden_states)
+        residual = hidden_states
+        hidden_states = self.mlp(normed)
+        return residual + hidden_states
+
+    forward.__wrapped__ = orig
+    return forward
+
+
+def _qwen3_attention_forward(orig):
+    """Qwen3Attention.forward (modeling_qwen3.py) with q_norm / k_norm and
+    apply_rotary_pos_emb as one rms_norm_rope over the projections' [B, S,
+    H, D] views; everything else is the original's code path."""
+    mod = importlib.import_module(orig.__module__)
+
+    def forward(self, hidden_states, position_embeddings, attention_mask,
+                past_key_values=None, **kwargs):
+        cos, sin = position_embeddings
+        qn, kn = self.q_norm, self.k_norm
+        wq, wk = _norm_weight(qn, hidden_states), _norm_weight(kn, hidden_states)
+        tables_need_grad = torch.is_grad_enabled() and (cos.requires_grad or sin.requires_grad)
+        if (wq is None or wk is None or qn.variance_epsilon != kn.variance_epsilon
+                or tables_need_grad or not _fusable(cos, sin) or cos.dtype != hidden_states.dtype
+                or sin.dtype != cos.dtype):
+            return orig(self, hidden_states, position_embeddings, attention_mask,
+                        past_key_values, **kwargs)
+        input_shape = hidden_states.shape[:-1]
+        hidden_shape = (*input_shape, -1, self.head_dim)
+        q = self.q_proj(hidden_states).view(hidden_shape)          # [B, S, Hq, D]
+        k = self.k_proj(hidden_states).view(hidden_shape)          # [B, S, Hkv, D]
+        value_states = self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+        q, k = ops.rms_norm_rope(q, k, wq, wk, cos, sin, qn.variance_epsilon, 2, _rounding)
+        query_states, key_states = q.transpose(1, 2), k.transpose(1, 2)
+        if past_key_values is not None:
+            key_states, value_states = past_key_values.update(key_states, value_states,
+                                                              self.layer_idx)
+        attention_interface = mod.ALL_ATTENTION_FUNCTIONS.get_interface(
+            self.config._attn_implementation, mod.eager_attention_forward)
+        attn_output, attn_weights = attention_interface(
+            self, query_states, key_states, value_states, attention_mask,
+            dropout=0.0 if not self.training else self.attention_dropout,
+            scaling=self.scaling, sliding_window=self.sliding_window, **kwargs)
+        attn_output = attn_output.reshape(*input_shape, -1).contiguous()
+        return self.o_proj(attn_output), attn_weights
+
+    forward.__wrapped__ = orig
+    return forward
+
+
 def enable_hf_fused_ops(models=tuple(_MODEL_FILES), rounding: Optional[str] = None) -> list:
     """Patch the installed transformers model files; returns what was patched."""
     global _rounding
@@ -136,11 +229,14 @@ def enable_hf_fused_ops(models=tuple(_MODEL_FILES), rounding: Optional[str] = No
             mod = importlib.import_module(f"transformers.models.{name}.modeling_{name}")
         except Exception:
             continue
-        norm_cls, mlp_cls = _MODEL_FILES[name]
+        norm_cls, mlp_cls, layer_cls, attn_cls = _MODEL_FILES[name]
         targets = [(getattr(mod, norm_cls, None), "forward", _rms_forward),
                    (getattr(mod, mlp_cls, None), "forward", _mlp_forward),
                    (mod, "apply_rotary_pos_emb", _rope_fn),
-                   (mod, "eager_attention_forward", _attention_fn)]
+                   (mod, "eager_attention_forward", _attention_fn),
+                   (getattr(mod, layer_cls, None), "forward", _decoder_forward)]
+        if attn_cls is not None:
+            targets.append((getattr(mod, attn_cls, None), "forward", _qwen3_attention_forward))
         for owner, attr, make in targets:
             if owner is None or not hasattr(owner, attr):
                 continue

@@ -42,8 +42,9 @@ def test_qwen3_forward_on_flagos_matches_cpu():
     torch.testing.assert_close(out.cpu(), ref, rtol=1e-3, atol=1e-3)
 
 
-def test_qwen3_forward_with_fused_hooks(monkeypatch):
-    calls = {"rms_norm": 0, "rope_qk": 0, "swiglu": 0, "masked_softmax": 0}
+def _count_fused_calls(monkeypatch):
+    calls = {n: 0 for n in ("rms_norm", "rope_qk", "swiglu", "masked_softmax", "add_rms_norm",
+                            "rms_norm_rope")}
     for name in calls:
         orig = getattr(torch_fl.ops, name)
 
@@ -52,6 +53,11 @@ def test_qwen3_forward_with_fused_hooks(monkeypatch):
             return _orig(*a, **k)
 
         monkeypatch.setattr(torch_fl.ops, name, counted)
+    return calls
+
+
+def test_qwen3_forward_with_fused_hooks(monkeypatch):
+    calls = _count_fused_calls(monkeypatch)
     model = tiny_qwen3(torch.float32)
     ids = torch.randint(0, 512, (2, 48), generator=torch.Generator().manual_seed(2))
     with torch.no_grad():
@@ -59,11 +65,46 @@ def test_qwen3_forward_with_fused_hooks(monkeypatch):
         model_d = model.to("flagos:0")
         patched = torch_fl.enable_hf_fused_ops()
         assert any("apply_rotary_pos_emb" in p for p in patched)
+        assert any("Qwen3Attention" in p for p in patched)
         out = model_d(ids.to("flagos:0")).logits
-    # 2 layers x (input + post-attention + q_norm + k_norm) + final norm
-    assert calls["rms_norm"] >= 9 and calls["rope_qk"] == 2 and calls["swiglu"] == 2, calls
-    assert calls["masked_softmax"] == 2, calls     # eager attention, one per layer
+    # per layer: input_layernorm; q_norm + k_norm + RoPE as one rms_norm_rope;
+    # the residual add + post_attention_layernorm as one add_rms_norm; the
+    # MLP's SwiGLU; the eager attention tail.  Plus the final norm.
+    assert calls["rms_norm_rope"] == 2 and calls["rope_qk"] == 0, calls
+    assert calls["add_rms_norm"] == 2 and calls["rms_norm"] == 3, calls
+    assert calls["swiglu"] == 2 and calls["masked_softmax"] == 2, calls
     torch.testing.assert_close(out.cpu(), ref, rtol=1e-3, atol=1e-3)
+
+
+def tiny_llama(dtype):
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    cfg = LlamaConfig(vocab_size=512, hidden_size=256, intermediate_size=704,
+                      num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                      head_dim=64, max_position_embeddings=256, rms_norm_eps=1e-5,
+                      attn_implementation="eager")
+    torch.manual_seed(0)
+    return LlamaForCausalLM(cfg).to(dtype).eval()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_llama_forward_with_fused_hooks(monkeypatch, dtype):
+    """Llama has no q/k norms: RoPE stays one rope_qk per layer, the residual
+    add + post_attention_layernorm is one add_rms_norm."""
+    calls = _count_fused_calls(monkeypatch)
+    model = tiny_llama(dtype)
+    ids = torch.randint(0, 512, (2, 40), generator=torch.Generator().manual_seed(5))
+    with torch.no_grad():
+        model_d = model.to("flagos:0")
+        ref = model_d(ids.to("flagos:0")).logits.float().cpu()   # unhooked, on flagos
+        torch_fl.enable_hf_fused_ops(rounding="chain")
+        out = model_d(ids.to("flagos:0")).logits.float().cpu()
+    assert calls["rope_qk"] == 2 and calls["rms_norm_rope"] == 0, calls
+    assert calls["add_rms_norm"] == 2 and calls["rms_norm"] == 3, calls
+    if dtype == torch.float32:
+        torch.testing.assert_close(out, ref, rtol=1e-3, atol=1e-3)
+    else:
+        assert (out - ref).abs().max() <= 0.05 * ref.abs().max()
 
 
 @pytest.mark.parametrize("hooks", [True, False])

@@ -473,9 +473,22 @@ def main():
                     help="launch without programmatic dependent launch (the default uses it)")
     ap.add_argument("--profile-case", choices=sorted(PROFILE_CASES),
                     help="run one small case of one op once on GPU 0 and exit (for ncu)")
+    ap.add_argument("--op-configs-only", action="store_true",
+                    help="time only the per-op configurations on GPU 0 and print them")
+    ap.add_argument("--case", default=None,
+                    help="regular expression: time only the per-op configurations it matches")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args.profile_case)
+        return
+    if args.op_configs_only:
+        import torch_fl  # noqa: F401
+        from torch_fl import _abi
+
+        _abi.set_pdl(not args.no_pdl)
+        torch.cuda.set_device(0)
+        print(json.dumps({"per_op_configs": op_configs(torch.device("cuda", 0),
+                                                       measured_peak()[0], only=args.case)}))
         return
     assert args.warmup >= 3 or os.environ.get("FL_B200_BENCH_ALLOW_SHORT"), "use --warmup >= 3"
 
@@ -751,7 +764,7 @@ def main():
     if world == 1 and not args.no_op_configs:
         del stack.g, stack.u, stack.a        # room for the 17 GB softmax config
         torch.cuda.empty_cache()
-        per_op_configs = op_configs(dev, measured_peak()[0])
+        per_op_configs = op_configs(dev, measured_peak()[0], only=args.case)
 
     if rank == 0:
         cpu = None
@@ -785,7 +798,7 @@ def main():
         dist.destroy_process_group()
 
 
-def op_configs(dev, peak, reps=5):
+def op_configs(dev, peak, reps=5, only=None):
     """Per-op HBM GB/s on the other benchmark configurations (device time,
     CUDA events, median of `reps` after 2 warm-ups; inputs resident, each
     larger than L2 except the 67 MB RMSNorm f32 config, which L2 holds)."""
@@ -802,7 +815,11 @@ def op_configs(dev, peak, reps=5):
     flush_rd = torch.ones(64 << 20, dtype=torch.float32, device=dev)
     flush_sink = torch.empty((), dtype=torch.float32, device=dev)
 
+    import re
+
     def timed(name, fn, nbytes, note="", flush=False, tokens=None, reps_=None):
+        if only and not re.search(only, name):
+            return
         for _ in range(2):
             fn()
         torch.cuda.synchronize()
@@ -831,7 +848,13 @@ def op_configs(dev, peak, reps=5):
         if note:
             out[name]["note"] = note
 
-    chain_configs(dev, g, timed)
+    def want(*names):
+        return only is None or any(re.search(only, n) for n in names)
+
+    if want("llama_chain_T8192", "rms_norm_bf16_8192x4096", "rope_qk_bf16_T8192",
+            "swiglu_bf16_8192x14336", "add_bf16_8192x4096", "rms_norm_rope_bf16_T8192",
+            "rms_norm_rope_bf16_T131072"):
+        chain_configs(dev, g, timed)
 
     # config 1: RMSNorm fp32 [2048, 4096], eps 1e-6
     x = torch.randn(2048, 4096, generator=g, device=dev)
@@ -842,6 +865,9 @@ def op_configs(dev, peak, reps=5):
     # config 3: causal softmax
     for dt, L, name in ((torch.bfloat16, 2048, "bf16_8x32x2048x2048"),
                         (torch.float16, 4096, "f16_8x32x4096x4096")):
+        if not want(f"softmax_{name}", f"causal_softmax_{name}", f"softmax_{name}_f32_out",
+                    f"masked_softmax_{name}", f"masked_softmax_{name}_torch_chain"):
+            continue
         lg = (3.0 * torch.randn(8, 32, L, L, generator=g, device=dev)).to(dt)
         masked = lg.masked_fill(torch.triu(torch.ones(L, L, dtype=torch.bool, device=dev), 1),
                                 float("-inf"))
@@ -1061,6 +1087,8 @@ PROFILE_CASES = {
     "softmax_long": "softmax bf16 [512, 128256] (a vocabulary of logits per row)",
     "elementwise": "add bf16 [32768, 4096] + [32768, 4096]; mul by a [4096] row vector; "
                    "mul by a [32768, 1] column",
+    "masked_softmax_f16_4096": "scaled masked softmax f16 [1, 32, 4096, 4096], HF mask "
+                               "[1, 1, 4096, 4096]",
     "chain_8192": "the 8192-token Llama chain: RMSNorm [8192, 4096], RoPE q [8192, 32, 128] / "
                   "k [8192, 8, 128], SwiGLU [8192, 14336], residual add [8192, 4096]; then "
                   "Qwen3 q/k-norm -> RoPE on the same q, k",
@@ -1124,6 +1152,12 @@ def profile_case(name):
                       K.swiglu(gt, up, out=a), K.add(x, y, out=h),
                       K.rope_qk(q, k, cos, sin, layout="bshd", q_weight=wq, k_weight=wk,
                                 eps=1e-6, q_out=qo, k_out=ko))
+    elif name == "masked_softmax_f16_4096":
+        x = (3.0 * torch.randn(1, 32, 4096, 4096, generator=g, device=dev)).to(torch.float16)
+        m = torch.zeros(1, 1, 4096, 4096, dtype=torch.float16, device=dev).masked_fill(
+            torch.triu(torch.ones(4096, 4096, dtype=torch.bool, device=dev), 1),
+            torch.finfo(torch.float16).min)
+        fn = lambda: K.masked_softmax(x, m, 128 ** -0.5)  # noqa: E731
     elif name == "masked_softmax":
         x = (3.0 * torch.randn(2, 32, 2048, 2048, generator=g, device=dev)).to(torch.bfloat16)
         m = torch.zeros(2, 1, 2048, 2048, dtype=torch.bfloat16, device=dev).masked_fill(

@@ -563,11 +563,26 @@ int launch_softmax(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
 // Row r of x (viewed [B, H, Q, K]) is query i = r % Q of head h = (r / Q) % H
 // in batch b = r / (Q*H); its mask row starts at b*sb + h*sh + i*sq elements
 // (a stride of 0 broadcasts, e.g. HF's [B, 1, Q, K] mask over the heads).
+//
+// Visit order (head_inner, used by softmax_masked_pair_kernel): with the
+// mask broadcast over the heads (sh == 0, HF's [B, 1, Q, K] mask) rows are
+// walked query by query with the heads of one query next to each other
+// (visit index v = (b*Q + i)*H + h), so the H rows that share a mask row run
+// together and the mask row is reused from L2 within a few rows rather than
+// a whole head (~96 MB of other traffic at [8, 32, 4096, 4096] f16) later.
+// (For the four-warp kernel this order measured the same as row order.)
 struct MaskRows {
   int64_t heads, q_len, sb, sh, sq;
+  bool head_inner;
   __device__ __forceinline__ int64_t offset(int64_t row) const {
     const int64_t i = row % q_len, t = row / q_len;
     return (t / heads) * sb + (t % heads) * sh + i * sq;
+  }
+  // Row of x / y visited at position v.
+  __device__ __forceinline__ int64_t row_of(int64_t v) const {
+    if (!head_inner) return v;
+    const int64_t h = v % heads, t = v / heads;  // t = b*Q + i
+    return ((t / q_len) * heads + h) * q_len + (t % q_len);
   }
 };
 
@@ -630,10 +645,10 @@ softmax_masked_kernel(const TI* __restrict__ x, int64_t ldx, const TI* __restric
   const uint64_t scale2 = f2_make(scale, scale);
   for (int64_t base = (int64_t)blockIdx.x * RPB; base < rows;
        base += (int64_t)gridDim.x * RPB) {
-    const int64_t row = base + slot;
-    const bool ok = row < rows;
+    const bool ok = base + slot < rows;
+    const int64_t row = ok ? mg.row_of(base + slot) : 0;
     const TI* xr = x + row * ldx;
-    const TI* mr = MASK ? mask + mg.offset(ok ? row : 0) : nullptr;
+    const TI* mr = MASK ? mask + mg.offset(row) : nullptr;
     uint4 xv[VPT], mv[VPT];
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -712,6 +727,185 @@ softmax_masked_kernel(const TI* __restrict__ x, int64_t ldx, const TI* __restric
   }
 }
 
+// 16-byte asynchronous copy global -> shared (cp.async, bypassing L1) and
+// its group commit / wait (the wait returns once this thread's committed
+// copies have landed: a hardware wait on the thread's own copies).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
+// Rows of 257..512 packs (e.g. 4096 f16 keys): two warps per row, 8 packs
+// of x and 8 of the mask per lane, turned into fp32 logits in registers as
+// in softmax_masked_kernel.  Each warp takes its half's max m_w and the sum
+// s_w of exp(logit - m_w) over its own exps; the pair then exchanges (m_w,
+// s_w) once through shared memory, behind a named barrier for those two
+// warps only (bar.sync 1 + slot, 64), and combines
+//   M = max(m_a, m_b),  S = sum_w s_w * 2^((m_w - M) log2e),
+// each warp storing its exps times c_w = 2^((m_w - M) log2e) / S.  So a row
+// costs one barrier of two warps, and the four rows of a CTA never wait for
+// each other (a persistent grid: each pair walks its own rows).  The
+// per-warp factor changes a result by a few fp32 ulp against the one-max
+// form.  A half whose keys are all -inf has s_w = 0 and c_w = 0; a row with
+// no visible key gets S = 0 and comes out NaN, as in the reference.
+//
+// The packs come through shared memory one row ahead: as soon as a thread
+// has its row in registers it issues cp.async copies of its next row's x and
+// mask packs into the same slots (its own slots only, so no barrier), and
+// the copies stream in while the row is reduced, exponentiated and stored.
+// Registers hold one row; shared memory (64 KB a CTA) holds the next.
+// Measured on B200, f16 [8, 32, 4096, 4096] with the [8, 1, 4096, 4096] HF
+// mask: 2.95 ms (5.91 TB/s); the same kernel loading from global memory
+// directly 3.19 ms (3.10 ms at 3 CTAs per SM, which spills); the four-warp
+// rows it replaces (4 packs of x and mask per thread, two CTA-wide barriers
+// per row) 3.47 ms; one warp per row holding only x and reading the mask
+// again per pass spilled at 128 registers, and staging x in shared memory
+// for that geometry was issue-bound at 12 warps per SM (5.9 ms).
+constexpr int kPairVPT = 8;  // packs per lane: rows of up to 2 * 32 * 8 = 512 packs
+
+template <typename TI, typename TO, bool MASK, bool CHAIN, bool W32>
+__global__ void __launch_bounds__(256, 2)
+softmax_masked_pair_kernel(const TI* __restrict__ x, int64_t ldx, const TI* __restrict__ mask,
+                           MaskRows mg, TO* __restrict__ y, int64_t ldy, int64_t rows, int nvec,
+                           float scale) {
+  constexpr int VW = Elem<TI>::kVec;
+  constexpr int NP = VW / 2;
+  constexpr int RPB = 4;  // rows (warp pairs) per CTA
+  __shared__ float2 part[RPB][2][2];  // [slot][row parity][warp of the pair] = (m_w, s_w)
+  // each thread's x and mask packs of its next row, [pack][thread] so that a
+  // warp's 16-byte accesses are consecutive (no bank conflicts)
+  extern __shared__ uint4 stage[];
+  const int slot = threadIdx.x >> 6;
+  const int half = (threadIdx.x >> 5) & 1;
+  const int lane = threadIdx.x & 63;  // lane within the row's 64 threads
+  const uint64_t scale2 = f2_make(scale, scale);
+  const uint64_t log2e2 = f2_make(kLog2e, kLog2e);
+  const int64_t stride = (int64_t)gridDim.x * RPB;
+  const auto issue = [&](int64_t vrow) {
+    const int64_t r = mg.row_of(vrow);
+    const TI* xr = x + r * ldx;
+    const TI* mr = MASK ? mask + mg.offset(r) : nullptr;
+#pragma unroll
+    for (int i = 0; i < kPairVPT; ++i) {
+      const int vi = lane + i * 64;
+      if (vi < nvec) {
+        cp_async16(&stage[i * 256 + threadIdx.x], xr + (int64_t)vi * VW);
+        if constexpr (MASK)
+          cp_async16(&stage[(kPairVPT + i) * 256 + threadIdx.x], mr + (int64_t)vi * VW);
+      }
+    }
+    cp_async_commit();
+  };
+  if ((int64_t)blockIdx.x * RPB + slot < rows) issue((int64_t)blockIdx.x * RPB + slot);
+  int parity = 0;
+  for (int64_t base = (int64_t)blockIdx.x * RPB; base < rows; base += stride, parity ^= 1) {
+    if (base + slot >= rows) break;  // uniform over the pair
+    const int64_t row = mg.row_of(base + slot);
+    uint4 xv[kPairVPT], mv[kPairVPT];
+    cp_async_wait_all();  // this row's copies (issued one row ahead) landed
+#pragma unroll
+    for (int i = 0; i < kPairVPT; ++i) {
+      const bool in = lane + i * 64 < nvec;
+      xv[i] = in ? stage[i * 256 + threadIdx.x] : make_uint4(0, 0, 0, 0);
+      if constexpr (MASK) mv[i] = in ? stage[(kPairVPT + i) * 256 + threadIdx.x]
+                                     : neg_inf_pack<TI>();
+      else mv[i] = in ? make_uint4(0, 0, 0, 0) : neg_inf_pack<TI>();
+    }
+    uint64_t v[kPairVPT][NP];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kPairVPT; ++i) {
+      float f[VW], mk[VW];
+      unpack<TI>(xv[i], f);
+      unpack<TI>(mv[i], mk);
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        const uint64_t xp = f2_make(f[2 * p], f[2 * p + 1]);
+        const uint64_t mp = f2_make(mk[2 * p], mk[2 * p + 1]);
+        if constexpr (CHAIN) {
+          v[i][p] = round_pair<TI>(f2_add(round_pair<TI>(f2_mul(xp, scale2)), mp));
+        } else {
+          v[i][p] = f2_fma(xp, scale2, mp);
+        }
+        m = fmax3(m, f2_lo(v[i][p]), f2_hi(v[i][p]));
+      }
+    }
+    // the next row's packs go into the slots just read (each thread reuses
+    // only its own slots, after its values are in registers)
+    if (base + stride + slot < rows) issue(base + stride + slot);
+    m = group_reduce_warp<FastMaxOp, 32>(m);
+    // exps against this warp's max: the one-FMA form, (logit - m) first for
+    // a max below -2.36e38 (wide_max), and a zero shift for an all -inf half
+    // (its exps are then exact zeros, not NaN)
+    const float mw = (m == -INFINITY) ? 0.f : m;
+    if (wide_max(mw)) {
+      const uint64_t nm2 = f2_make(-mw, -mw);
+#pragma unroll
+      for (int i = 0; i < kPairVPT; ++i)
+#pragma unroll
+        for (int p = 0; p < NP; ++p) v[i][p] = f2_mul(f2_add(v[i][p], nm2), log2e2);
+    } else {
+      const uint64_t nml2 = f2_make(-mw * kLog2e, -mw * kLog2e);
+#pragma unroll
+      for (int i = 0; i < kPairVPT; ++i)
+#pragma unroll
+        for (int p = 0; p < NP; ++p) v[i][p] = f2_fma(v[i][p], log2e2, nml2);
+    }
+    uint64_t acc = f2_make(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < kPairVPT; ++i) {
+#pragma unroll
+      for (int p = 0; p < NP; ++p)
+        v[i][p] = f2_make(ex2_approx(f2_lo(v[i][p])), ex2_approx(f2_hi(v[i][p])));
+      uint64_t t[NP];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) t[p] = v[i][p];
+#pragma unroll
+      for (int w = NP / 2; w >= 1; w /= 2)
+#pragma unroll
+        for (int p = 0; p < w; ++p) t[p] = f2_add(t[p], t[p + w]);
+      acc = f2_add(acc, t[0]);
+    }
+    float sw = f2_lo(acc) + f2_hi(acc);
+    sw = group_reduce_warp<SumOp, 32>(sw);
+    // the pair's exchange (double-buffered by row parity: the partner has
+    // read this buffer's previous values before it reached the barrier of
+    // the row in between)
+    if ((threadIdx.x & 31) == 0) part[slot][parity][half] = make_float2(m, sw);
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + slot) : "memory");
+    const float2 o = part[slot][parity][half ^ 1];
+    const float M = fmaxf(m, o.x);
+    // the scale of each half's exps against the row max (0 for an all -inf
+    // half; for a wide row m - M is exact, Sterbenz)
+    const float fw = (m == -INFINITY) ? 0.f : ex2_approx((m - M) * kLog2e);
+    const float fo = (o.x == -INFINITY) ? 0.f : ex2_approx((o.x - M) * kLog2e);
+    const float S = sw * fw + o.y * fo;
+    const float c = fw / S;
+    const uint64_t c2 = f2_make(c, c);
+    TO* yr = y + row * ldy;
+#pragma unroll
+    for (int i = 0; i < kPairVPT; ++i) {
+      const int vi = lane + i * 64;
+      if (vi >= nvec) continue;
+      float out[VW];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        const uint64_t t = f2_mul(v[i][p], c2);
+        out[2 * p] = f2_lo(t);
+        out[2 * p + 1] = f2_hi(t);
+      }
+      store_vals<TO, VW, W32>(yr + (int64_t)vi * VW, out);
+    }
+  }
+  cp_async_wait_all();
+}
+
 // Any row length / alignment: one CTA per row, three passes over the row
 // (the second and third mostly from L2).
 template <typename TI, typename TO, bool MASK, bool CHAIN>
@@ -719,7 +913,8 @@ __global__ void __launch_bounds__(256)
 softmax_masked_loop_kernel(const TI* x, int64_t ldx, const TI* mask, MaskRows mg, TO* y,
                            int64_t ldy, int64_t rows, int64_t cols, float scale) {
   __shared__ float smem[256 / 32];
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+  for (int64_t v = blockIdx.x; v < rows; v += gridDim.x) {
+    const int64_t row = mg.row_of(v);
     const TI* xr = x + row * ldx;
     const TI* mr = MASK ? mask + mg.offset(row) : nullptr;
     const auto logit = [&](int64_t c) {
@@ -785,6 +980,29 @@ int launch_softmax_masked(const TI* x, int64_t ldx, const TI* mask, const MaskRo
         return launch_status();
       }
     };
+    if (nvec > 256 && nvec <= 512) {
+      // two warps per row, one pair exchange (softmax_masked_pair_kernel)
+      const auto pairs = [&](auto w32) -> int {
+        constexpr bool W = decltype(w32)::value;
+        auto kern = softmax_masked_pair_kernel<TI, TO, MASK, CHAIN, W>;
+        const size_t smem = (size_t)2 * kPairVPT * 256 * 16;  // 64 KB: x and mask packs
+        // (per device: a function attribute belongs to the current context)
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem) != cudaSuccess)
+          return launch_status();
+        static const int per_sm = blocks_per_sm(kern, 256, smem);
+        const int grid = (int)std::max<int64_t>(
+            1, std::min<int64_t>(ceil_div(rows, 4), (int64_t)per_sm * dev.sm_count));
+        MaskRows mgh = mg;
+        mgh.head_inner = MASK && mg.sh == 0 && mg.heads > 1;
+        kern<<<grid, 256, smem, stream>>>(x, ldx, mask, mgh, y, ldy, rows, (int)nvec, scale);
+        return launch_status();
+      };
+      if constexpr (std::is_same<TO, float>::value && VW == 8) {
+        if (aligned32(y) && ldy % 8 == 0) return pairs(std::true_type{});
+      }
+      return pairs(std::false_type{});
+    }
     int r = -1;
     if constexpr (std::is_same<TO, float>::value && VW == 8) {
       r = row_ladder<8>(nvec, go);
@@ -862,7 +1080,7 @@ FL_B200_API int fl_b200_softmax_masked(const void* x, int64_t ld_x, const void* 
   FLB_CHECK_ARG(rounding == FL_B200_ROUND_FUSED || rounding == FL_B200_ROUND_CHAIN);
   if (rows == 0 || cols == 0) return FL_B200_OK;
   FLB_CHECK_ARG(x && out && ld_x >= cols && ld_out >= cols);
-  const MaskRows mg{heads, q_len, mask_stride_b, mask_stride_h, mask_stride_q};
+  const MaskRows mg{heads, q_len, mask_stride_b, mask_stride_h, mask_stride_q, false};
   auto s = static_cast<cudaStream_t>(stream);
   return dispatch_in_out(in_dtype, out_dtype, [&](auto ti, auto to) -> int {
     using TI = decltype(ti);

@@ -84,6 +84,12 @@ def test_masked_softmax_matches_hf_eager_attention(golden):
     ((2, 2, 32, 128), "pad"),          # [B, 1, 1, K] padding-only mask
     ((1, 4, 32, 512), "none"),
     ((32, 256), "shared"),             # [Q, K] logits, [Q, K] mask
+    # rows of 257..512 packs: one warp per row, staged in shared memory
+    ((2, 4, 16, 4096), "hf"),          # HF mask, padding queries at the lowest value
+    ((1, 5, 8, 4096), "hf"),           # 5 heads: head-inner order across CTA warps
+    ((1, 3, 8, 2056), "full"),         # 257 packs (16-bit), a mask per head
+    ((2, 2, 8, 4096), "pad"),          # [B, 1, 1, K]: mask shared by heads and queries
+    ((1, 2, 8, 4096), "none"),
 ])
 def test_masked_softmax_fused_vs_oracle(dtype, shape, mask_kind):
     x = rnd(shape, dtype, 70, scale=4.0)

@@ -182,6 +182,43 @@ FL_B200_API int fl_b200_cast(const void* src, int src_dtype, void* dst,
                              int dst_dtype, int64_t n, fl_b200_stream_t stream);
 
 /* ------------------------------------------------------------------------ *
+ * The other ops of the HF formulas, reached when the fused hooks are off:  *
+ * one pass each, in the arithmetic of the reference's cuda route.          */
+typedef enum {
+  FL_B200_UNARY_SILU = 0,   /* x / (1 + exp(-x)) in fp32 (silu.cu:15-35)             */
+  FL_B200_UNARY_RSQRT = 1,  /* rsqrtf (rsqrt.cu:14-32)                               */
+  FL_B200_UNARY_NEG = 2,    /* -x; also int32/int64, two's complement (neg.cu:14-32) */
+  FL_B200_UNARY_COS = 3,    /* cosf (cos.cu:14-32)                                   */
+  FL_B200_UNARY_SIN = 4,    /* sinf (sin.cu:14-32)                                   */
+  FL_B200_UNARY_SQUARE = 5, /* pow(x, 2) = x*x (pow.cu:29-32)                        */
+  FL_B200_UNARY_CUBE = 6,   /* pow(x, 3) = x*x*x, the square rounded to the dtype    */
+  FL_B200_UNARY_POW = 7     /* powf(x, p), p already rounded to the dtype (pow.cu:25) */
+} fl_b200_unary_op;
+/* Rows of `cols` contiguous elements, row r starting at x + offset(r):     *
+ * r is split over row_sizes[0..row_ndim) (last fastest) and offset(r) is     *
+ * the sum of the parts times row_strides (elements; up to 4 dims once size-1 *
+ * dims are dropped and evenly stepping neighbours merged; HF's q[..., D/2:] *
+ * of a transposed q fits).  out[r, j] = op(x[offset(r) + j]), out dense.     *
+ * Replaces silu / rsqrt / neg / cos / sin / pow.Tensor_Scalar              *
+ * (csrc/aten/register.cc:405-417 -> csrc/aten/backends/cuda/silu.cu,       *
+ * rsqrt.cu, neg.cu, cos.cu, sin.cu, pow.cu).  Float dtypes; NEG also takes *
+ * I32/I64.                                                                  */
+FL_B200_API int fl_b200_unary(const void* x, const int64_t* row_sizes,
+                              const int64_t* row_strides, int row_ndim, int64_t cols, void* out,
+                              int op, double p, int dtype, fl_b200_stream_t stream);
+/* Concatenation as row blocks: out[r, off_k + j] = srcs[k][offset_k(r) + j] *
+ * for j < widths[k], off_k = widths[0] + ... + widths[k-1]; offset_k as in *
+ * fl_b200_unary with the shared row_sizes and input k's strides            *
+ * src_row_strides[k*row_ndim ..].  out dense: prod(row_sizes) rows of      *
+ * sum(widths) elements of elem_size bytes.  A cat along dim d is this with *
+ * row_sizes = the sizes before d and widths[k] = the product of input k's  *
+ * sizes from d on (contiguous within each input).  Replaces cat            *
+ * (csrc/aten/cat.cc:13-39 -> PyTorch's cat_out_cuda).                      */
+FL_B200_API int fl_b200_cat(const void* const* srcs, const int64_t* src_row_strides,
+                            const int64_t* widths, int n_inputs, const int64_t* row_sizes,
+                            int row_ndim, void* out, int elem_size, fl_b200_stream_t stream);
+
+/* ------------------------------------------------------------------------ *
  * Softmax over the last dim with fp32 accumulation, replacing _softmax      *
  * (register.cc:270-272 -> csrc/aten/backends/cuda/softmax.cc:14-40).       *
  * in_dtype F32/BF16/F16; out_dtype = in_dtype, or F32 (half_to_float).     *

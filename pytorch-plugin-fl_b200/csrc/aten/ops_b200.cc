@@ -169,6 +169,159 @@ at::Tensor SiluBackwardB200(const at::Tensor& grad, const at::Tensor& self) {
   return dx;
 }
 
+// ------------------------------------------------ the other HF formula ops --
+// silu / rsqrt / neg / cos / sin / pow.Tensor_Scalar / cat on this library's
+// kernels (unary.cu), in the arithmetic of the reference's cuda route
+// (csrc/aten/register.cc:405-417).  A dtype the kernels do not take (integer
+// tensors, except neg on int32/int64) runs PyTorch's CUDA kernel on the same
+// memory, which is what the op's cuda route runs.
+
+// Sizes and strides of the dims before `split`, when the dims from `split`
+// on are contiguous in x: the rows of fl_b200_unary / fl_b200_cat.
+bool OuterDims(const at::Tensor& x, int64_t split, std::vector<int64_t>& sizes,
+               std::vector<int64_t>& strides) {
+  int64_t expect = 1;
+  for (int64_t d = x.dim() - 1; d >= split; --d) {
+    if (x.size(d) != 1 && x.stride(d) != expect) return false;
+    expect *= x.size(d);
+  }
+  sizes.assign(x.sizes().begin(), x.sizes().begin() + split);
+  strides.assign(x.strides().begin(), x.strides().begin() + split);
+  return true;
+}
+
+using AtenUnary = at::Tensor (*)(const at::Tensor&);
+
+at::Tensor UnaryB200(const at::Tensor& self, int op, double p, const char* name,
+                     AtenUnary cuda_op) {
+  const at::ScalarType t = self.scalar_type();
+  const int code = B200Dtype(t);
+  const bool takes = IsFloat(t) || (op == FL_B200_UNARY_NEG && code >= 0);
+  if (!takes) return ToFlagos(cuda_op(CudaAlias(self)));
+  GpuGuard g(self);
+  at::Tensor x = self;
+  if (x.dim() > 0 && !x.is_non_overlapping_and_dense()) {
+    std::vector<int64_t> sz, st;
+    if (x.stride(-1) == 1 && OuterDims(x, x.dim() - 1, sz, st)) {
+      // rows of the last dim, placed by the outer dims; the output dense
+      at::Tensor out = at::empty(x.sizes(), x.options());
+      if (x.numel() == 0) return out;
+      CheckB200(fl_b200_unary(x.data_ptr(), sz.data(), st.data(), (int)sz.size(), x.size(-1),
+                              out.data_ptr(), op, p, code, StreamOf(x)),
+                name);
+      return out;
+    }
+    x = x.contiguous();
+  }
+  // a dense layout in any dim order: one flat pass, the output keeps the strides
+  at::Tensor out = at::empty_strided(x.sizes(), x.strides(), x.options());
+  if (x.numel() == 0) return out;
+  CheckB200(fl_b200_unary(x.data_ptr(), nullptr, nullptr, 0, x.numel(), out.data_ptr(), op, p,
+                          code, StreamOf(x)),
+            name);
+  return out;
+}
+
+at::Tensor SiluB200(const at::Tensor& x) {
+  return UnaryB200(x, FL_B200_UNARY_SILU, 0.0, "silu", [](const at::Tensor& t) {
+    return at::silu(t);
+  });
+}
+at::Tensor RsqrtB200(const at::Tensor& x) {
+  return UnaryB200(x, FL_B200_UNARY_RSQRT, 0.0, "rsqrt", [](const at::Tensor& t) {
+    return at::rsqrt(t);
+  });
+}
+at::Tensor NegB200(const at::Tensor& x) {
+  return UnaryB200(x, FL_B200_UNARY_NEG, 0.0, "neg", [](const at::Tensor& t) {
+    return at::neg(t);
+  });
+}
+at::Tensor CosB200(const at::Tensor& x) {
+  return UnaryB200(x, FL_B200_UNARY_COS, 0.0, "cos", [](const at::Tensor& t) {
+    return at::cos(t);
+  });
+}
+at::Tensor SinB200(const at::Tensor& x) {
+  return UnaryB200(x, FL_B200_UNARY_SIN, 0.0, "sin", [](const at::Tensor& t) {
+    return at::sin(t);
+  });
+}
+
+// pow(tensor, scalar): the exponent converted to the tensor's dtype first,
+// then 2 -> x*x, 3 -> x*x*x, else pow (pow.cu:15-46).
+at::Tensor PowScalarB200(const at::Tensor& self, const at::Scalar& e) {
+  const at::ScalarType t = self.scalar_type();
+  if (!IsFloat(t) || e.isComplex()) return ToFlagos(at::pow(CudaAlias(self), e));
+  double ed;
+  if (t == at::kBFloat16) ed = static_cast<float>(e.to<at::BFloat16>());
+  else if (t == at::kHalf) ed = static_cast<float>(e.to<at::Half>());
+  else ed = e.to<float>();
+  const int op = ed == 2.0 ? FL_B200_UNARY_SQUARE
+                           : (ed == 3.0 ? FL_B200_UNARY_CUBE : FL_B200_UNARY_POW);
+  return UnaryB200(self, op, ed, "pow.Tensor_Scalar", nullptr);
+}
+
+// cat: inputs of one dtype on one flagos device as row blocks (fl_b200_cat);
+// anything else (dtype promotion, a mismatch to report) goes to PyTorch's cat.
+at::Tensor CatB200(const at::ITensorListRef& tensors, int64_t dim) {
+  const char* name = "cat";
+  std::vector<at::Tensor> all;
+  for (const at::Tensor& t : tensors) all.push_back(t);
+  auto cuda_cat = [&]() {
+    std::vector<at::Tensor> v;
+    for (const at::Tensor& t : all) v.push_back(CudaAlias(t));
+    return ToFlagos(at::cat(v, dim));
+  };
+  // legacy empty tensors (1-D, size 0) take no part, as in PyTorch
+  std::vector<at::Tensor> ts;
+  for (const at::Tensor& t : all)
+    if (!(t.dim() == 1 && t.size(0) == 0)) ts.push_back(t);
+  if (ts.empty() || all.empty()) return cuda_cat();
+  const at::Tensor& t0 = ts[0];
+  const int64_t nd = t0.dim();
+  if (nd == 0) return cuda_cat();
+  const int64_t d = at::maybe_wrap_dim(dim, nd);
+  // a byte copy: any dtype of 1, 2, 4 or 8 bytes
+  if (!t0.is_privateuseone() || t0.element_size() > 8) return cuda_cat();
+  int64_t cat_size = 0;
+  for (const at::Tensor& t : ts) {
+    if (t.dim() != nd || t.scalar_type() != t0.scalar_type() || t.device() != t0.device())
+      return cuda_cat();
+    for (int64_t i = 0; i < nd; ++i)
+      if (i != d && t.size(i) != t0.size(i)) return cuda_cat();  // its error message
+    cat_size += t.size(d);
+  }
+  std::vector<int64_t> shape(t0.sizes().begin(), t0.sizes().end());
+  shape[d] = cat_size;
+  at::Tensor out = at::empty(shape, t0.options());
+  if (out.numel() == 0) return out;
+  std::vector<at::Tensor> keep;  // contiguous copies of inputs the kernel cannot read
+  std::vector<const void*> srcs;
+  std::vector<int64_t> widths, strides;
+  std::vector<int64_t> row_sizes(t0.sizes().begin(), t0.sizes().begin() + d);
+  for (const at::Tensor& t0k : ts) {
+    at::Tensor t = t0k;
+    std::vector<int64_t> sz, st;
+    if (!OuterDims(t, d, sz, st)) {
+      keep.push_back(t.contiguous());
+      t = keep.back();
+      OuterDims(t, d, sz, st);
+    }
+    srcs.push_back(t.data_ptr());
+    strides.insert(strides.end(), st.begin(), st.end());
+    int64_t w = 1;  // the input's elements per row: its sizes from d on
+    for (int64_t i = d; i < nd; ++i) w *= t.size(i);
+    widths.push_back(w);
+  }
+  GpuGuard g(out);
+  CheckB200(fl_b200_cat(srcs.data(), strides.data(), widths.data(), (int)srcs.size(),
+                        row_sizes.data(), (int)row_sizes.size(), out.data_ptr(),
+                        (int)t0.element_size(), StreamOf(out)),
+            name);
+  return out;
+}
+
 // ------------------------------------------------------------- reductions --
 enum class Red { kSum, kMean, kAmax, kArgmax };
 
@@ -359,5 +512,12 @@ FLB_REGISTER_KERNEL(ArgmaxFn, argmax_dispatcher, Backend::kB200, ArgmaxB200)
 FLB_REGISTER_KERNEL(SoftmaxBackwardFn, softmax_backward_dispatcher, Backend::kB200,
                     SoftmaxBackwardB200)
 FLB_REGISTER_KERNEL(SiluBackwardFn, silu_backward_dispatcher, Backend::kB200, SiluBackwardB200)
+FLB_REGISTER_KERNEL(UnaryFn, silu_dispatcher, Backend::kB200, SiluB200)
+FLB_REGISTER_KERNEL(UnaryFn, rsqrt_dispatcher, Backend::kB200, RsqrtB200)
+FLB_REGISTER_KERNEL(UnaryFn, neg_dispatcher, Backend::kB200, NegB200)
+FLB_REGISTER_KERNEL(UnaryFn, cos_dispatcher, Backend::kB200, CosB200)
+FLB_REGISTER_KERNEL(UnaryFn, sin_dispatcher, Backend::kB200, SinB200)
+FLB_REGISTER_KERNEL(PowScalarFn, pow_tensor_scalar_dispatcher, Backend::kB200, PowScalarB200)
+FLB_REGISTER_KERNEL(CatFn, cat_dispatcher, Backend::kB200, CatB200)
 
 }  // namespace flb200::aten

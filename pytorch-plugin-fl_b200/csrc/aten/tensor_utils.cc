@@ -1,5 +1,6 @@
 #include "tensor_utils.h"
 
+#include <ATen/Context.h>
 #include <c10/core/TensorImpl.h>
 
 namespace flb200::aten {
@@ -7,6 +8,11 @@ namespace flb200::aten {
 at::Tensor Rewrap(const at::Tensor& t, c10::DeviceType target) {
   if (!t.defined() || t.device().type() == target || t.device().is_cpu()) return t;
   TORCH_CHECK(t.layout() == c10::kStrided, "flagos: only strided tensors are supported");
+  // A CUDA alias is about to meet PyTorch's CUDA kernels, which allocate
+  // through CUDA's caching allocator: make sure PyTorch's lazy CUDA set-up has
+  // run (a process whose first op on flagos has no flagos kernel has not
+  // touched CUDA through PyTorch yet).  A no-op after the first call.
+  if (target == c10::DeviceType::CUDA) at::globalContext().lazyInitDevice(c10::DeviceType::CUDA);
   const c10::Storage& src = t.storage();
   const c10::Device dev(target, t.device().index());
   // The new storage points at the same bytes; its context owns a reference

@@ -77,7 +77,9 @@ rms_norm_bwd_kernel(const T* __restrict__ dy, int64_t lddy, const T* __restrict_
   uint4 xv[VPT], gv[VPT];
   int64_t base = (int64_t)blockIdx.x * RPB;
   load(base + slot, xv, gv);
-  for (; base < rows; base += (int64_t)gridDim.x * RPB) {
+  __shared__ float2 sums[TPR > 32 ? 2 * BLOCK / 32 : 1];
+  int parity = 0;
+  for (; base < rows; base += (int64_t)gridDim.x * RPB, parity ^= 1) {
     const int64_t row = base + slot;
     const bool ok = row < rows;
     uint4 xn[VPT], gn[VPT];
@@ -96,8 +98,13 @@ rms_norm_bwd_kernel(const T* __restrict__ dy, int64_t lddy, const T* __restrict_
         tx = fmaf(wf[e] * gf[e], xf[e], tx);
       }
     }
-    ss = row_reduce<SumOp, TPR, BLOCK>(ss, red);
-    tx = row_reduce<SumOp, TPR, BLOCK>(tx, red);
+    if constexpr (TPR > 32) {
+      // both sums in one exchange among the row's warps (named barrier)
+      row_sum2_named<TPR, BLOCK>(ss, tx, sums, parity);
+    } else {
+      ss = row_reduce<SumOp, TPR, BLOCK>(ss, red);
+      tx = row_reduce<SumOp, TPR, BLOCK>(tx, red);
+    }
     const float r = 1.0f / sqrtf(ss / cols_f + eps);
     const float m = tx * r / cols_f;
 #pragma unroll
@@ -191,12 +198,77 @@ rms_norm_bwd_loop_kernel(const T* dy, int64_t lddy, const T* x, int64_t ldx, con
   }
 }
 
-// dw[c] = sum over p < P of partial[p][c], p in order; 32 columns x 8
-// chunks of p per CTA, the chunks added in order through shared memory.
+// dw[c] = sum over p < P of partial[p][c] in a fixed order.  A CTA covers 32
+// columns as 8 float4 lanes x 32 chunks of the partial rows; each thread
+// keeps 4 independent running sums per column over its chunk (the loads of
+// a chunk in flight together: the partials come from L2, so the time is
+// latency, not bytes), then the 32 chunks are added in chunk order through
+// shared memory.  Measured on B200 (296 partial rows x 4096 columns, fp32):
+// the previous one-load-at-a-time form took 15.7 us.
 template <typename T>
 __global__ void __launch_bounds__(256)
 rms_norm_dw_reduce_kernel(const float* __restrict__ partial, int64_t P, int64_t cols,
                           T* __restrict__ dw) {
+  __shared__ float4 s[32][9];
+  const int q = threadIdx.x & 7, ch = threadIdx.x >> 3;  // float4 lane, chunk
+  const int64_t c = (int64_t)blockIdx.x * 32 + q * 4;     // first of 4 columns
+  const int64_t per = ceil_div(P, 32);
+  const int64_t p0 = ch * per, p1 = min(P, p0 + per);
+  float4 acc[4] = {};
+  if (c < cols) {  // cols % 4 == 0 (the vector path), so c + 3 < cols too
+    int64_t p = p0;
+    for (; p + 3 < p1; p += 4) {
+      float4 v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        v[k] = *reinterpret_cast<const float4*>(partial + (p + k) * cols + c);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        acc[k].x += v[k].x;
+        acc[k].y += v[k].y;
+        acc[k].z += v[k].z;
+        acc[k].w += v[k].w;
+      }
+    }
+    for (; p < p1; ++p) {
+      const float4 v = *reinterpret_cast<const float4*>(partial + p * cols + c);
+      acc[0].x += v.x;
+      acc[0].y += v.y;
+      acc[0].z += v.z;
+      acc[0].w += v.w;
+    }
+  }
+  float4 t = acc[0];
+#pragma unroll
+  for (int k = 1; k < 4; ++k) {
+    t.x += acc[k].x;
+    t.y += acc[k].y;
+    t.z += acc[k].z;
+    t.w += acc[k].w;
+  }
+  s[ch][q] = t;
+  __syncthreads();
+  if (ch == 0 && c < cols) {
+    float4 r = s[0][q];
+    for (int k = 1; k < 32; ++k) {
+      r.x += s[k][q].x;
+      r.y += s[k][q].y;
+      r.z += s[k][q].z;
+      r.w += s[k][q].w;
+    }
+    dw[c] = Elem<T>::from_f(r.x);
+    dw[c + 1] = Elem<T>::from_f(r.y);
+    dw[c + 2] = Elem<T>::from_f(r.z);
+    dw[c + 3] = Elem<T>::from_f(r.w);
+  }
+}
+
+// The same for any column count (the scalar backward's partial rows): one
+// column per thread, 8 chunks of the partial rows added in chunk order.
+template <typename T>
+__global__ void __launch_bounds__(256)
+rms_norm_dw_reduce_scalar_kernel(const float* __restrict__ partial, int64_t P, int64_t cols,
+                                 T* __restrict__ dw) {
   __shared__ float s[8][33];
   const int cl = threadIdx.x & 31, ch = threadIdx.x >> 5;
   const int64_t c = (int64_t)blockIdx.x * 32 + cl;
@@ -256,8 +328,13 @@ int launch_rms_norm_bwd(const T* dy, int64_t lddy, const T* x, int64_t ldx, cons
     st = launch_status();
   }
   if (st != FL_B200_OK || dw == nullptr) return st;
-  rms_norm_dw_reduce_kernel<T><<<(int)ceil_div(cols, 32), 256, 0, stream>>>(partial, used,
-                                                                            cols, dw);
+  if (cols % 4 == 0 && aligned16(partial)) {
+    rms_norm_dw_reduce_kernel<T><<<(int)ceil_div(cols, 32), 256, 0, stream>>>(partial, used,
+                                                                              cols, dw);
+  } else {
+    rms_norm_dw_reduce_scalar_kernel<T><<<(int)ceil_div(cols, 32), 256, 0, stream>>>(
+        partial, used, cols, dw);
+  }
   return launch_status();
 }
 

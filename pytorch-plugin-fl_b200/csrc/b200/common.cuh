@@ -333,6 +333,37 @@ __device__ __forceinline__ float row_reduce(float v, float* smem) {
   }
 }
 
+// Sums of a and b over the TPR threads of a row (TPR a multiple of 32, the
+// row's warps consecutive, BLOCK / TPR <= 15 rows per CTA) with one barrier
+// of the row's own warps instead of CTA-wide ones: each warp's pair of sums
+// goes to its slot of `buf` (float2[2 * BLOCK / 32], two halves used by
+// alternate rows through `parity`), the row's warps meet at named barrier
+// 1 + row slot, and every thread adds the row's partials in warp order (so
+// all of them get the same sums).  The halves alternate so that a warp's
+// write for its next row cannot overwrite values its partners still read:
+// they have passed the barrier of the row in between.
+template <int TPR, int BLOCK>
+__device__ __forceinline__ void row_sum2_named(float& a, float& b, float2* buf, int parity) {
+  static_assert(TPR % 32 == 0 && BLOCK / TPR <= 15, "row_sum2_named geometry");
+  constexpr int W = TPR / 32;
+  a = group_reduce_warp<SumOp, 32>(a);
+  b = group_reduce_warp<SumOp, 32>(b);
+  const int warp = threadIdx.x >> 5;
+  const int slot = threadIdx.x / TPR;
+  float2* half = buf + parity * (BLOCK / 32);
+  if ((threadIdx.x & 31) == 0) half[warp] = make_float2(a, b);
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + slot), "r"(TPR) : "memory");
+  const float2* row = half + slot * W;
+  float2 t = row[0];
+#pragma unroll
+  for (int i = 1; i < W; ++i) {
+    t.x += row[i].x;
+    t.y += row[i].y;
+  }
+  a = t.x;
+  b = t.y;
+}
+
 // Whole-CTA reduction; the result is valid in every thread.
 template <typename Op, int BLOCK>
 __device__ __forceinline__ float block_reduce(float v, float* smem) {

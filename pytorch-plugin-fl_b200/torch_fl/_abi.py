@@ -17,6 +17,9 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libf
 F32, BF16, F16, I32, I64 = 0, 1, 2, 3, 4
 # rounding policy (fl_b200_rounding)
 ROUND_FUSED, ROUND_CHAIN = 0, 1
+# fl_b200_unary_op
+UNARY_SILU, UNARY_RSQRT, UNARY_NEG, UNARY_COS, UNARY_SIN, UNARY_SQUARE, UNARY_CUBE, UNARY_POW = \
+    range(8)
 
 _p = C.c_void_p
 _i64 = C.c_int64
@@ -53,6 +56,8 @@ PROTOTYPES: dict[str, tuple] = {
     "fl_b200_mul": (_i32, [_p, _pi64, _p, _pi64, _p, _pi64, _i32, _i32, _p]),
     "fl_b200_binary_scalar": (_i32, [_p, _f64, _p, _i64, _i32, _f64, _i32, _p]),
     "fl_b200_cast": (_i32, [_p, _i32, _p, _i32, _i64, _p]),
+    "fl_b200_unary": (_i32, [_p, _pi64, _pi64, _i32, _i64, _p, _i32, _f64, _i32, _p]),
+    "fl_b200_cat": (_i32, [C.POINTER(_p), _pi64, _pi64, _i32, _pi64, _i32, _p, _i32, _p]),
     "fl_b200_softmax_lastdim": (
         _i32, [_p, _i64, _p, _i64, _i64, _i64, _i32, _i32, _i32, _i64, _i64, _p]),
     "fl_b200_softmax_middim": (_i32, [_p, _p, _i64, _i64, _i64, _i32, _i32, _p]),

@@ -360,6 +360,75 @@ def masked_softmax(x: torch.Tensor, mask: torch.Tensor | None = None, scale: flo
     return out.view(x.shape)
 
 
+# --------------------------------------------- the other HF formula ops
+_UNARY = {"silu": _abi.UNARY_SILU, "rsqrt": _abi.UNARY_RSQRT, "neg": _abi.UNARY_NEG,
+          "cos": _abi.UNARY_COS, "sin": _abi.UNARY_SIN}
+
+
+def _outer(x: torch.Tensor, split: int):
+    """(sizes, strides) of x's dims before `split` when its dims from `split`
+    on are contiguous, else None."""
+    expect = 1
+    for d in range(x.dim() - 1, split - 1, -1):
+        if x.size(d) != 1 and x.stride(d) != expect:
+            return None
+        expect *= x.size(d)
+    return list(x.shape[:split]), list(x.stride()[:split])
+
+
+def unary(x: torch.Tensor, op: str, exponent: float = 0.0) -> torch.Tensor:
+    """silu / rsqrt / neg / cos / sin of x, or pow(x, exponent) (op "pow";
+    the exponent rounded to x's dtype first, 2 and 3 as products, as the
+    reference's cuda route computes them) through fl_b200_unary.  x's rows of
+    the last dim may be strided (any outer dims); the result is dense."""
+    if op == "pow":
+        e = float(torch.tensor(exponent, dtype=x.dtype)) if x.is_floating_point() else exponent
+        code = _abi.UNARY_SQUARE if e == 2.0 else (_abi.UNARY_CUBE if e == 3.0 else _abi.UNARY_POW)
+    else:
+        e, code = 0.0, _UNARY[op]
+    view = _outer(x, x.dim() - 1) if x.dim() else ([], [])
+    if view is None:
+        x = x.contiguous()
+        view = _outer(x, x.dim() - 1)
+    sizes, strides = view
+    out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    if out.numel():
+        with _on_device(x):
+            _abi.call("fl_b200_unary", x.data_ptr(), _abi.i64_array(sizes),
+                      _abi.i64_array(strides), len(sizes), x.shape[-1] if x.dim() else 1,
+                      out.data_ptr(), code, float(e), dtype_code(x), _stream(x))
+    return out
+
+
+def cat(tensors, dim: int = 0) -> torch.Tensor:
+    """torch.cat(tensors, dim) for tensors of one dtype through fl_b200_cat
+    (row blocks; each input's dims from `dim` on contiguous, any outer
+    strides)."""
+    t0 = tensors[0]
+    d = dim % t0.dim()
+    shape = list(t0.shape)
+    shape[d] = sum(t.shape[d] for t in tensors)
+    out = torch.empty(shape, dtype=t0.dtype, device=t0.device)
+    srcs, strides, widths, keep = [], [], [], []
+    for t in tensors:
+        v = _outer(t, d)
+        if v is None:
+            t = t.contiguous()
+            keep.append(t)
+            v = _outer(t, d)
+        srcs.append(t.data_ptr())
+        strides += v[1]
+        widths.append(int(torch.tensor(t.shape[d:]).prod()) if d < t.dim() else 1)
+    if out.numel():
+        import ctypes as C
+        arr = (C.c_void_p * len(srcs))(*srcs)
+        with _on_device(t0):
+            _abi.call("fl_b200_cat", arr, _abi.i64_array(strides), _abi.i64_array(widths),
+                      len(srcs), _abi.i64_array(shape[:d]), d, out.data_ptr(),
+                      t0.element_size(), _stream(t0))
+    return out
+
+
 # ------------------------------------------------------------------ reductions
 def _workspace(rows: int, cols: int, device) -> torch.Tensor | None:
     n = _abi.lib().fl_b200_reduce_workspace_size(rows, cols)

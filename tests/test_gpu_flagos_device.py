@@ -256,6 +256,17 @@ def test_dispatch_log_cuda_override():
     assert "[flagos dispatch] _softmax -> cuda" in r.stderr
 
 
+def test_first_op_through_the_cuda_fallback_in_a_fresh_process():
+    # an op with no flagos kernel (abs, cumsum) as the process's first op on
+    # flagos: PyTorch's CUDA kernel runs on aliases and must find CUDA set up
+    code = ("import torch_fl, torch; x = torch.randn(4, 8).to('flagos:0'); "
+            "y = x.abs().cumsum(-1); torch.flagos.synchronize(); "
+            "assert torch.allclose(y.cpu(), x.cpu().abs().cumsum(-1), rtol=1e-5, atol=1e-6); "
+            "print('ok')")
+    r = _run(code, {})
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr
+
+
 def test_unbuilt_backend_is_an_error():
     r = _run(SOFTMAX, {"FLAGOS_OP__softmax": "flaggems"})
     assert r.returncode != 0

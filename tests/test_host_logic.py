@@ -39,12 +39,16 @@ def _routes(env=None):
 
 
 def test_default_config_routes_the_op_set_to_b200():
+    # every routed op of the path, the HF formula ops included, runs on the
+    # b200 kernels with the shipped config; no op is configured `= cuda`
     routes, _ = _routes()
     for op in ["add.Tensor", "mul.Tensor", "_softmax", "sum.dim_IntList", "mean.dim", "amax",
-               "argmax"]:
+               "argmax", "silu", "rsqrt", "neg", "cos", "sin", "pow.Tensor_Scalar", "cat",
+               "_softmax_backward_data", "silu_backward"]:
         assert routes[op] == "b200", (op, routes[op])
-    for op in ["silu", "rsqrt", "neg", "cos", "sin", "pow.Tensor_Scalar", "cat"]:
-        assert routes[op] == "cuda", (op, routes[op])
+    conf = os.path.join(ROOT, "pytorch-plugin-fl_b200", "torch_fl", "backends.conf")
+    lines = [ln.split("#")[0].strip() for ln in open(conf)]
+    assert not [ln for ln in lines if ln.replace(" ", "").endswith("=cuda")]
 
 
 def test_env_override_and_custom_config(tmp_path):
@@ -59,12 +63,13 @@ def test_env_override_and_custom_config(tmp_path):
     assert routes["mul.Tensor"] == "b200"           # unknown backend ignored -> default
     assert "unknown backend 'nonsense'" in err
     assert routes["amax"] == "b200"                 # unlisted op with a b200 kernel
-    assert routes["cat"] == "cuda"                  # unlisted op without one
+    assert routes["cat"] == "b200"                  # every routed op has one
 
 
 def test_missing_config_falls_back_to_defaults(tmp_path):
     routes, _ = _routes({"FLAGOS_BACKEND_CONFIG": str(tmp_path / "absent.conf")})
-    assert routes["_softmax"] == "b200" and routes["neg"] == "cuda"
+    # no config: every op with a b200 kernel (all routed ops) runs on b200
+    assert routes["_softmax"] == "b200" and routes["neg"] == "b200"
 
 
 def test_missing_kernel_library_fails_loudly(tmp_path):
@@ -147,3 +152,4 @@ def test_hf_hooks_install_and_leave_cpu_tensors_alone():
         torch_fl.disable_hf_fused_ops()
     assert mq.eager_attention_forward is orig
     assert torch.equal(out, ref)
+

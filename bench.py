@@ -728,11 +728,37 @@ def main():
                 torch.cuda.synchronize()
                 best = min(best, c0.elapsed_time(c1))
             rates[name] = round(nbytes / (best / 1e3) / 1e9, 1)
-        del tmp
+        # The floor the host sets: one step's copy in and copy out running at
+        # the same time on their two streams, every rank at once (as in the
+        # e2e step).  With many ranks sharing the host's links and memory,
+        # this, not the GPU, can bound the e2e step.
+        tmp2 = torch.empty_like(stack.x0)
+        barrier()
+        floor = float("inf")
+        for _ in range(2):
+            f0 = torch.cuda.Event(enable_timing=True)
+            f1 = torch.cuda.Event(enable_timing=True)
+            f2 = torch.cuda.Event(enable_timing=True)
+            f0.record(comp)
+            h2d.wait_event(f0)
+            d2h.wait_event(f0)
+            with flagos.stream(h2d):
+                tmp.copy_(h_in, non_blocking=True)
+            with flagos.stream(d2h):
+                h_out.copy_(tmp2, non_blocking=True)
+            f1.record(h2d)
+            f2.record(d2h)
+            torch.cuda.synchronize()
+            floor = min(floor, max(f0.elapsed_time(f1), f0.elapsed_time(f2)))
+        floor = sharding.max_over_ranks(floor, dev)
+        del tmp, tmp2
         e2e = {"value": args.tokens * args.steps / (ems / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": nbytes * world, "d2h_bytes_per_step": nbytes * world,
                "ms_per_step": ems / args.steps, "matches_device_path": same,
                "chunks": chunks, "host_copy_gbs": rates,
+               "copy_floor_ms": round(floor, 3),
+               "copy_floor_what": "one step's host->device and device->host copies at the same "
+                                  "time on two streams, all ranks at once (max over ranks)",
                "api": "torch_fl.ops (flagos:: ops) on flagos tensors, host<->flagos copies "
                       "on flagos streams overlapping the layers"}
 
@@ -1087,6 +1113,8 @@ PROFILE_CASES = {
     "softmax_long": "softmax bf16 [512, 128256] (a vocabulary of logits per row)",
     "elementwise": "add bf16 [32768, 4096] + [32768, 4096]; mul by a [4096] row vector; "
                    "mul by a [32768, 1] column",
+    "causal_softmax_f16_4096": "causal softmax f16 [1, 32, 4096, 4096] (mask applied in the "
+                               "kernel)",
     "masked_softmax_f16_4096": "scaled masked softmax f16 [1, 32, 4096, 4096], HF mask "
                                "[1, 1, 4096, 4096]",
     "chain_8192": "the 8192-token Llama chain: RMSNorm [8192, 4096], RoPE q [8192, 32, 128] / "
@@ -1152,6 +1180,9 @@ def profile_case(name):
                       K.swiglu(gt, up, out=a), K.add(x, y, out=h),
                       K.rope_qk(q, k, cos, sin, layout="bshd", q_weight=wq, k_weight=wk,
                                 eps=1e-6, q_out=qo, k_out=ko))
+    elif name == "causal_softmax_f16_4096":
+        x = (3.0 * torch.randn(1, 32, 4096, 4096, generator=g, device=dev)).to(torch.float16)
+        fn = lambda: K.softmax(x, causal=True)  # noqa: E731
     elif name == "masked_softmax_f16_4096":
         x = (3.0 * torch.randn(1, 32, 4096, 4096, generator=g, device=dev)).to(torch.float16)
         m = torch.zeros(1, 1, 4096, 4096, dtype=torch.float16, device=dev).masked_fill(

@@ -477,13 +477,15 @@ def test_softmax_row_rungs(dtype, cols):
     assert torch.isnan(got[:, :3]).all() and not torch.isnan(got[:, 3:]).any()
 
 
+@pytest.mark.parametrize("cols", [2048, 4096])
 @pytest.mark.parametrize("causal", [False, True])
-def test_softmax_f32_out_both_store_widths(causal):
+def test_softmax_f32_out_both_store_widths(causal, cols):
     """fp32 output of 16-bit rows goes out as 32-byte stores when the output
-    is 32-byte aligned and as 16-byte stores otherwise; both match the oracle."""
+    is 32-byte aligned and as 16-byte stores otherwise; both match the oracle
+    (4096 keys: the causal rows run two warps a row, staged one row ahead)."""
     from torch_fl import _abi
 
-    rows, cols = 96, 2048
+    rows = 96
     x = rnd((rows, cols), torch.bfloat16, 41, scale=3.0)
     ref = ops.softmax_golden(parity.to_np(x).reshape(1, rows, cols), "f32", causal=causal)
     ref = ref.reshape(rows, cols)
@@ -559,6 +561,29 @@ def test_causal_softmax_full_size():
         parity.assert_ulp(parity.to_np(b[bi, hi]), ref, "bf16", 1, f"slice {bi},{hi}")
     s = b.float().sum(-1)
     assert torch.allclose(s, torch.ones_like(s), atol=2e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_causal_softmax_4096_keys(dtype):
+    """Causal rows of 4096 16-bit keys (two warps a row, one (max, sum)
+    exchange, the visible packs staged one row ahead): every query of 2 x 8
+    heads against the oracle, and the in-kernel mask against the same
+    logits masked beforehand."""
+    B, H, L = 2, 8, 4096
+    dt = parity.dname(dtype)
+    g = torch.Generator(device=DEV).manual_seed(35)
+    x = (3.0 * torch.randn(B, H, L, L, generator=g, device=DEV)).to(dtype)
+    got = K.softmax(x, causal=True)
+    for bi, hi in [(0, 0), (1, 7), (0, 5)]:
+        ref = ops.softmax_golden(parity.to_np(x[bi, hi]), dt, causal=True)
+        parity.assert_ulp(parity.to_np(got[bi, hi]), ref, dt, 1, f"slice {bi},{hi}")
+    masked = torch.triu(torch.ones(L, L, dtype=torch.bool, device=DEV), 1)
+    assert (got[:, :, masked] == 0).all()            # masked keys: exact zeros
+    plain = K.softmax(x.masked_fill(masked, float("-inf")))
+    # probabilities are >= 0, so 16-bit patterns order like the values: the
+    # ulp distance is the difference of the patterns
+    d = (got.view(torch.int16).int() - plain.view(torch.int16).int()).abs().max().item()
+    assert d <= 1, d
 
 
 # ---------------------------------------------------------------- reductions

@@ -465,6 +465,8 @@ def main():
                     help="token chunks per e2e step: host->device copies, the layers and the "
                          "device->host copies of different chunks overlap on three flagos streams")
     ap.add_argument("--no-eager", action="store_true")
+    ap.add_argument("--no-hf-e2e", action="store_true",
+                    help="skip the HF decoder-model leg (hidden states host -> flagos -> host)")
     ap.add_argument("--eager-layers", type=int, default=4)
     ap.add_argument("--no-op-configs", action="store_true")
     ap.add_argument("--no-graph", action="store_true",
@@ -675,8 +677,10 @@ def main():
         # device->host copy before queueing step s, as a serving loop bounds
         # its queue (device memory then stays at two steps' buffers).
         inflight = []
+        host_s = [0.0]   # host time spent issuing steps (not waiting on `inflight`)
 
         def e2e_step():
+            t_issue = time.perf_counter()
             for lo, hi in bounds:
                 with flagos.stream(h2d):
                     x_d = h_in[lo:hi].to(fdev, non_blocking=True)
@@ -694,21 +698,35 @@ def main():
             ev = flagos.Event()
             ev.record(d2h)
             inflight.append(ev)
+            host_s[0] += time.perf_counter() - t_issue
             if len(inflight) > 2:
                 inflight.pop(0).synchronize()
 
-        for _ in range(max(args.warmup, 3)):
+        # Warm-up until the flagos allocator's pool has settled: its blocks
+        # are reused only on the stream that freed them, and the steps in
+        # flight hold blocks on three streams; measured on B200, the pool was
+        # still growing (by 805 MB) in the 8 steps after 4 warm-up steps.
+        for _ in range(max(args.warmup, 8)):
             e2e_step()
         comp.wait_stream(d2h)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        em = torch.cuda.Event(enable_timing=True)
+        host_s[0] = 0.0
         e0.record(comp)
-        for _ in range(args.steps):
+        for i in range(args.steps):
             e2e_step()
+            if i == args.steps // 2 - 1:
+                em.record(comp)        # the first half's layers are queued before em
         comp.wait_stream(d2h)          # the last chunk is in host memory at e1
         e1.record(comp)
         torch.cuda.synchronize()
         ems = sharding.max_over_ranks(e0.elapsed_time(e1), dev)
+        halves = [ems / args.steps] * 2
+        if args.steps >= 2:
+            halves = [sharding.max_over_ranks(e0.elapsed_time(em), dev) / (args.steps // 2),
+                      sharding.max_over_ranks(em.elapsed_time(e1), dev)
+                      / (args.steps - args.steps // 2)]
         # the e2e result equals the device-resident path's result
         same = bool(torch.equal(h_out.to(dev), stack.run(stack.x0)))
         nbytes = h_in.numel() * h_in.element_size()
@@ -756,11 +774,22 @@ def main():
                "h2d_bytes_per_step": nbytes * world, "d2h_bytes_per_step": nbytes * world,
                "ms_per_step": ems / args.steps, "matches_device_path": same,
                "chunks": chunks, "host_copy_gbs": rates,
+               "ms_per_step_halves": [round(h, 3) for h in halves],
                "copy_floor_ms": round(floor, 3),
+               "host_issue_ms_per_step": round(
+                   sharding.max_over_ranks(host_s[0] * 1e3, dev) / args.steps, 3),
                "copy_floor_what": "one step's host->device and device->host copies at the same "
                                   "time on two streams, all ranks at once (max over ranks)",
                "api": "torch_fl.ops (flagos:: ops) on flagos tensors, host<->flagos copies "
                       "on flagos streams overlapping the layers"}
+
+    # A real HF model through the public API: hidden states from pinned host
+    # memory into a Llama-3-8B-shaped decoder (HF's own modules on flagos),
+    # the last hidden state back, with the fused-op hooks on and off;
+    # informational (the GEMMs dominate), N=1 only.
+    e2e_hf = None
+    if not args.no_hf_e2e and world == 1:
+        e2e_hf = hf_model_e2e(dev, args)
 
     # PyTorch's own CUDA kernels on the HF formulas (the kernels the
     # reference's cuda route runs), same stack, `eager_layers` layers timed
@@ -811,7 +840,7 @@ def main():
                                       else "eager launches"},
             "hbm_gbs_step": round(stack_bytes(stack) * args.steps / (ms / 1e3) / 1e9, 1),
             "per_op": per_op, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "pdl_ab": pdl_ab,
+            "pdl_ab": pdl_ab, "e2e_hf": e2e_hf,
             "gpu_eager_reference": eager, "per_op_configs": per_op_configs,
             "gpu_launches": stack.launches_per_step() * args.steps,
             "per_kernel_pass_ms_per_step": round(timed_pass_ms, 3),
@@ -822,6 +851,66 @@ def main():
         import torch.distributed as dist
 
         dist.destroy_process_group()
+
+
+def hf_model_e2e(dev, args, layers=2, batch=4, seq=2048, steps=5):
+    """transformers' LlamaModel (Llama-3-8B shapes: hidden 4096, 32 / 8 heads
+    of 128, intermediate 14336, eps 1e-5, theta 1e4, eager attention) with
+    `layers` random-init bf16 decoder layers on flagos.  One step: the
+    [batch, seq, 4096] hidden states copied from pinned host memory, the
+    forward (causal), the last hidden state copied back to pinned host
+    memory; device time per step (CUDA events), with the fused-op hooks
+    (torch_fl.enable_hf_fused_ops) and without them (HF's op chain on the
+    flagos aten routes)."""
+    import torch_fl
+    from transformers import LlamaConfig, LlamaModel
+
+    cfg = LlamaConfig(vocab_size=128, hidden_size=HIDDEN, intermediate_size=INTER,
+                      num_hidden_layers=layers, num_attention_heads=HQ, num_key_value_heads=HKV,
+                      head_dim=HEAD, max_position_embeddings=seq, rms_norm_eps=EPS,
+                      rope_parameters={"rope_type": "default", "rope_theta": THETA},
+                      attn_implementation="eager")
+    torch.manual_seed(0)
+    fdev = torch.device("flagos", dev.index)
+    model = LlamaModel(cfg).to(torch.bfloat16).to(fdev).eval()   # ~6 s of CPU init
+    g = torch.Generator().manual_seed(3)
+    h_in = torch.randn(batch, seq, HIDDEN, generator=g).to(torch.bfloat16).pin_memory()
+    h_out = torch.empty_like(h_in).pin_memory()
+
+    def step():
+        x = h_in.to(fdev, non_blocking=True)
+        y = model(inputs_embeds=x).last_hidden_state
+        h_out.copy_(y, non_blocking=True)
+
+    res = {}
+    outs = {}
+    for hooks in (True, False):
+        if hooks:
+            torch_fl.enable_hf_fused_ops()
+        with torch.no_grad():
+            for _ in range(2):
+                step()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                step()
+            e1.record()
+            torch.cuda.synchronize()
+        outs[hooks] = h_out.clone()
+        torch_fl.disable_hf_fused_ops()
+        ms = e0.elapsed_time(e1) / steps
+        res["hooks_on" if hooks else "hooks_off"] = {
+            "ms_per_step": round(ms, 3), "tokens_per_s": round(batch * seq / (ms / 1e3), 1)}
+    a, b = outs[True].float(), outs[False].float()
+    res["max_abs_diff_on_vs_off"] = round((a - b).abs().max().item(), 5)
+    res["max_abs_out"] = round(b.abs().max().item(), 3)
+    res.update({"model": f"transformers LlamaModel, {layers} decoder layers of Llama-3-8B shape, "
+                         "random init, bf16, eager attention", "batch": batch, "seq": seq,
+                "h2d_bytes_per_step": h_in.numel() * 2, "d2h_bytes_per_step": h_out.numel() * 2})
+    del model
+    torch.cuda.empty_cache()
+    return res
 
 
 def op_configs(dev, peak, reps=5, only=None):

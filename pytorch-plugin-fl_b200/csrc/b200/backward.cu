@@ -30,8 +30,9 @@ namespace {
 // A second kernel adds the partial rows in CTA order.  Both orders are
 // fixed, so dw does not depend on timing.  The next row's x and dy are
 // loaded while the current row is reduced and stored (two row buffers in
-// registers, 3 CTAs per SM): measured on B200, bf16 [65536, 4096] 5.73 vs
-// 5.44 TB/s with one buffer at 4 CTAs per SM.  Rows of 257..512 packs run
+// registers, 3 CTAs per SM; for 4096-wide 16-bit rows the next row goes to
+// shared memory instead, STAGE): measured on B200, bf16 [65536, 4096] 5.73
+// vs 5.44 TB/s with one buffer at 4 CTAs per SM.  Rows of 257..512 packs run
 // 128 threads x 4 packs (two rows per CTA) at 2 CTAs per SM: 6.12 vs 5.92
 // TB/s for 256 x 2 at 3 CTAs (bf16 4096-wide rows, kernel alone).
 constexpr int kBwdCtasPerSm = 3;
@@ -48,8 +49,8 @@ __host__ __device__ constexpr bool rms_bwd_slot_rows() {
   return RPB == 1 || (RPB == 2 && VPT >= 4);
 }
 
-template <typename T, int TPR, int VPT, int BLOCK>
-__global__ void __launch_bounds__(BLOCK, (rms_bwd_min_blocks<BLOCK, VPT>()))
+template <typename T, int TPR, int VPT, int BLOCK, bool STAGE, int MINB>
+__global__ void __launch_bounds__(BLOCK, MINB)
 rms_norm_bwd_kernel(const T* __restrict__ dy, int64_t lddy, const T* __restrict__ x,
                     int64_t ldx, const T* __restrict__ w, T* __restrict__ dx, int64_t lddx,
                     float* __restrict__ partial, int64_t rows, int nvec, float eps,
@@ -74,16 +75,48 @@ rms_norm_bwd_kernel(const T* __restrict__ dy, int64_t lddy, const T* __restrict_
       gv[i] = in ? ld_stream(dy + row * lddy + (int64_t)vi * VW) : make_uint4(0, 0, 0, 0);
     }
   };
+  // STAGE: the next row's x and dy packs copied into shared memory
+  // ([pack][thread]) by cp.async instead of held in a second set of registers
+  extern __shared__ uint4 stage[];
+  auto issue = [&](int64_t row) {
+    if (row < rows) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int vi = lane + i * TPR;
+        if (vi < nvec) {
+          cp_async16(&stage[i * BLOCK + threadIdx.x], x + row * ldx + (int64_t)vi * VW);
+          cp_async16(&stage[(VPT + i) * BLOCK + threadIdx.x], dy + row * lddy + (int64_t)vi * VW);
+        }
+      }
+    }
+    cp_async_commit();
+  };
+  auto take = [&](int64_t row, uint4 (&xv)[VPT], uint4 (&gv)[VPT]) {
+    cp_async_wait_all();
+    const bool ok = row < rows;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const bool in = ok && lane + i * TPR < nvec;
+      xv[i] = in ? stage[i * BLOCK + threadIdx.x] : make_uint4(0, 0, 0, 0);
+      gv[i] = in ? stage[(VPT + i) * BLOCK + threadIdx.x] : make_uint4(0, 0, 0, 0);
+    }
+  };
   uint4 xv[VPT], gv[VPT];
   int64_t base = (int64_t)blockIdx.x * RPB;
-  load(base + slot, xv, gv);
+  if constexpr (STAGE) issue(base + slot);
+  else load(base + slot, xv, gv);
   __shared__ float2 sums[TPR > 32 ? 2 * BLOCK / 32 : 1];
   int parity = 0;
   for (; base < rows; base += (int64_t)gridDim.x * RPB, parity ^= 1) {
     const int64_t row = base + slot;
     const bool ok = row < rows;
     uint4 xn[VPT], gn[VPT];
-    load(base + (int64_t)gridDim.x * RPB + slot, xn, gn);  // the next row, in flight meanwhile
+    if constexpr (STAGE) {
+      take(row, xv, gv);
+      issue(base + (int64_t)gridDim.x * RPB + slot);  // the next row, in flight meanwhile
+    } else {
+      load(base + (int64_t)gridDim.x * RPB + slot, xn, gn);  // the next row, in flight meanwhile
+    }
     float ss = 0.f, tx = 0.f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -123,12 +156,15 @@ rms_norm_bwd_kernel(const T* __restrict__ dy, int64_t lddy, const T* __restrict_
       }
       st_stream(dx + row * lddx + (int64_t)vi * VW, pack<T>(o));
     }
+    if constexpr (!STAGE) {
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      xv[i] = xn[i];
-      gv[i] = gn[i];
+      for (int i = 0; i < VPT; ++i) {
+        xv[i] = xn[i];
+        gv[i] = gn[i];
+      }
     }
   }
+  if constexpr (STAGE) cp_async_wait_all();
   if (partial == nullptr) return;
   if constexpr (rms_bwd_slot_rows<RPB, VPT>()) {
     // one partial row per row slot, in (CTA, slot) order
@@ -311,15 +347,28 @@ int launch_rms_norm_bwd(const T* dy, int64_t lddy, const T* x, int64_t ldx, cons
       const int64_t ctas =
           std::min<int64_t>(groups, (int64_t)dev.sm_count * rms_bwd_min_blocks<BLOCK, VPT>());
       used = ctas * (rms_bwd_slot_rows<RPB, VPT>() ? RPB : 1);
-      rms_norm_bwd_kernel<T, TPR, VPT, BLOCK><<<(int)ctas, BLOCK, 0, stream>>>(
-          dy, lddy, x, ldx, w, dx, lddx, partial, rows, (int)(cols / VW), eps, (float)cols);
+      rms_norm_bwd_kernel<T, TPR, VPT, BLOCK, false, rms_bwd_min_blocks<BLOCK, VPT>()>
+          <<<(int)ctas, BLOCK, 0, stream>>>(dy, lddy, x, ldx, w, dx, lddx, partial, rows,
+                                            (int)(cols / VW), eps, (float)cols);
       return launch_status();
     };
     const int64_t nvec = cols / VW;
-    if (nvec > 256 && nvec <= 512)
-      st = go(std::integral_constant<int, 128>{}, std::integral_constant<int, 4>{});
-    else
+    if (nvec > 256 && nvec <= 512) {
+      // 128 threads x 4 packs, two rows per CTA, 2 CTAs per SM, the next row's
+      // x and dy staged in shared memory (32 KB a CTA) by cp.async.  Measured on
+      // B200, bf16 [65536, 4096]: 0.257 ms against 0.263 with the next row in
+      // registers; 3 CTAs per SM (80 registers) spills and takes 0.278 ms.
+      constexpr int MINB = 2;
+      auto kern = rms_norm_bwd_kernel<T, 128, 4, 256, true, MINB>;
+      const size_t smem = (size_t)2 * 4 * 256 * 16;
+      const int64_t ctas = std::min<int64_t>(ceil_div(rows, 2), (int64_t)dev.sm_count * MINB);
+      used = ctas * 2;
+      kern<<<(int)ctas, 256, smem, stream>>>(dy, lddy, x, ldx, w, dx, lddx, partial, rows,
+                                             (int)nvec, eps, (float)cols);
+      st = launch_status();
+    } else {
       st = row_ladder<2>(nvec, go);
+    }
   }
   if (st < 0) {
     used = std::min<int64_t>(rows, (int64_t)dev.sm_count * kBwdCtasPerSm);

@@ -129,6 +129,20 @@ inline bool aligned32(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 31u) == 0;
 }
 
+// 16-byte asynchronous copy global -> shared (cp.async, bypassing L1) and
+// its group commit / wait (the wait returns once this thread's committed
+// copies have landed: a hardware wait on the thread's own copies).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 // Makes a pack opaque to the optimizer: after this the compiler cannot reuse
 // fp32 values it unpacked from `v` earlier, so a kernel that walks a row held
 // in registers twice keeps it packed (4 registers per 16 bytes) instead of

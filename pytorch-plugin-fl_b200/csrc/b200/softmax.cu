@@ -727,20 +727,6 @@ softmax_masked_kernel(const TI* __restrict__ x, int64_t ldx, const TI* __restric
   }
 }
 
-// 16-byte asynchronous copy global -> shared (cp.async, bypassing L1) and
-// its group commit / wait (the wait returns once this thread's committed
-// copies have landed: a hardware wait on the thread's own copies).
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-}
-
 // Rows of 257..512 packs (e.g. 4096 f16 keys): two warps per row, 8 packs
 // of x and 8 of the mask per lane, turned into fp32 logits in registers as
 // in softmax_masked_kernel.  Each warp takes its half's max m_w and the sum

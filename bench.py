@@ -703,11 +703,21 @@ def main():
                 inflight.pop(0).synchronize()
 
         # Warm-up until the flagos allocator's pool has settled: its blocks
-        # are reused only on the stream that freed them, and the steps in
-        # flight hold blocks on three streams; measured on B200, the pool was
-        # still growing (by 805 MB) in the 8 steps after 4 warm-up steps.
-        for _ in range(max(args.warmup, 8)):
+        # are reused only on the stream that freed them and the steps in
+        # flight hold blocks on three streams, so it grows for a while (on
+        # B200 from 8 to about 18 steps, run to run; a step that grows it is
+        # slow on the host).  At least `warmup` steps, then until two steps
+        # in a row leave the pool's reserved bytes unchanged (at most 40).
+        def reserved():  # host-side counter: no synchronisation (steps stay in flight)
+            return flagos.memory_stats().get("pool_reserved", 0)
+
+        warm, still, last = 0, 0, -1
+        while warm < 40 and (warm < max(args.warmup, 3) or still < 2):
             e2e_step()
+            warm += 1
+            now = reserved()
+            still = still + 1 if now == last else 0
+            last = now
         comp.wait_stream(d2h)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -775,6 +785,7 @@ def main():
                "ms_per_step": ems / args.steps, "matches_device_path": same,
                "chunks": chunks, "host_copy_gbs": rates,
                "ms_per_step_halves": [round(h, 3) for h in halves],
+               "warmup_steps": warm,
                "copy_floor_ms": round(floor, 3),
                "host_issue_ms_per_step": round(
                    sharding.max_over_ranks(host_s[0] * 1e3, dev) / args.steps, 3),

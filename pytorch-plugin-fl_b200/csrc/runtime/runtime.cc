@@ -2,6 +2,7 @@
 // stream-ordered caching allocator, the device guard and the hooks.
 #include "runtime.h"
 
+#include <ATen/Context.h>
 #include <ATen/core/CachingHostAllocator.h>
 #include <ATen/cuda/CUDAGeneratorImpl.h>
 #include <ATen/detail/PrivateUse1HooksInterface.h>
@@ -498,6 +499,12 @@ void init() {
   std::call_once(once, [] {
     c10::SetAllocator(c10::DeviceType::PrivateUse1, device_allocator());
     at::RegisterPrivateUse1HooksInterface(new Hooks());
+    // PyTorch answers is_pinned() through the current accelerator (flagos,
+    // once registered) and only for one it has marked initialised; pinned
+    // memory itself comes from the CUDA hooks, which mark CUDA, not flagos.
+    // Mark flagos too (its init is a no-op), so pinned host tensors report
+    // pinned.
+    at::globalContext().lazyInitDevice(c10::DeviceType::PrivateUse1);
   });
 }
 

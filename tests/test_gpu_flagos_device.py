@@ -256,6 +256,19 @@ def test_dispatch_log_cuda_override():
     assert "[flagos dispatch] _softmax -> cuda" in r.stderr
 
 
+def test_pinned_host_tensors_report_pinned():
+    a = torch.empty(1024, pin_memory=True)
+    assert a.is_pinned()
+    b = torch.randn(256).pin_memory()
+    assert b.is_pinned() and not torch.randn(8).is_pinned()
+    # a non-blocking copy from pinned memory into flagos and back
+    x = b.to("flagos:0", non_blocking=True)
+    out = torch.empty(256, pin_memory=True)
+    out.copy_(x, non_blocking=True)
+    torch.flagos.synchronize()
+    assert torch.equal(out, b)
+
+
 def test_first_op_through_the_cuda_fallback_in_a_fresh_process():
     # an op with no flagos kernel (abs, cumsum) as the process's first op on
     # flagos: PyTorch's CUDA kernel runs on aliases and must find CUDA set up

@@ -712,22 +712,24 @@ def main():
             return flagos.memory_stats().get("pool_reserved", 0)
 
         warm, still, last = 0, 0, -1
-        while warm < 40 and (warm < max(args.warmup, 3) or still < 2):
-            e2e_step()
-            warm += 1
-            now = reserved()
-            still = still + 1 if now == last else 0
-            last = now
+        with torch.inference_mode():
+            while warm < 40 and (warm < max(args.warmup, 3) or still < 2):
+                e2e_step()
+                warm += 1
+                now = reserved()
+                still = still + 1 if now == last else 0
+                last = now
         comp.wait_stream(d2h)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         em = torch.cuda.Event(enable_timing=True)
         host_s[0] = 0.0
         e0.record(comp)
-        for i in range(args.steps):
-            e2e_step()
-            if i == args.steps // 2 - 1:
-                em.record(comp)        # the first half's layers are queued before em
+        with torch.inference_mode():
+            for i in range(args.steps):
+                e2e_step()
+                if i == args.steps // 2 - 1:
+                    em.record(comp)    # the first half's layers are queued before em
         comp.wait_stream(d2h)          # the last chunk is in host memory at e1
         e1.record(comp)
         torch.cuda.synchronize()
@@ -791,8 +793,9 @@ def main():
                    sharding.max_over_ranks(host_s[0] * 1e3, dev) / args.steps, 3),
                "copy_floor_what": "one step's host->device and device->host copies at the same "
                                   "time on two streams, all ranks at once (max over ranks)",
-               "api": "torch_fl.ops (flagos:: ops) on flagos tensors, host<->flagos copies "
-                      "on flagos streams overlapping the layers"}
+               "api": "torch_fl.ops (flagos:: ops) on flagos tensors under "
+                      "torch.inference_mode, host<->flagos copies on flagos streams "
+                      "overlapping the layers"}
 
     # A real HF model through the public API: hidden states from pinned host
     # memory into a Llama-3-8B-shaped decoder (HF's own modules on flagos),
@@ -1017,6 +1020,14 @@ def op_configs(dev, peak, reps=5, only=None):
             lg * sc + hf, -1, dtype=torch.float32).to(dt), 4 * n + hf.numel() * 2,
             "the same tail as 4 PyTorch CUDA ops (bytes: the fused op's)")
         del lg, hf
+    if want("softmax_bf16_1024x128256", "softmax_f32_8192x32000"):
+        for dt, R, V in ((torch.bfloat16, 1024, 128256), (torch.float32, 8192, 32000)):
+            lv = (3.0 * torch.randn(R, V, generator=g, device=dev)).to(dt)
+            esz = lv.element_size()
+            timed(f"softmax_{'bf16' if dt == torch.bfloat16 else 'f32'}_{R}x{V}",
+                  lambda: K.softmax(lv), 2 * esz * lv.numel(), "vocabulary-long rows")
+            del lv
+
     # broadcast add / mul on the stack's activation shape: the residual add,
     # a [hidden] weight broadcast over the rows, a [T, 1] per-row scale
     TA = 131072

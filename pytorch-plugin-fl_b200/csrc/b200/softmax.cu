@@ -504,6 +504,221 @@ softmax_middim_kernel(const TI* x, TO* y, int64_t outer, int64_t n, int64_t inne
   }
 }
 
+// ---- rows split across a thread-block cluster ----------------------------
+// Rows of 4097..16384 packs (e.g. a 128256-entry vocabulary of bf16 logits),
+// too long for one CTA's registers: a cluster of C = 3..8 CTAs per row
+// (cluster size chosen at launch), each CTA holding 512 threads x 4 packs of
+// the row.  Each warp takes its max m_w and keeps its exponentials
+// exp(x - m_w) in registers (fp32) with their sum s_w; one CTA barrier later
+// warp 0 folds the warps' pairs into the CTA's (m_c, s_c) and publishes it
+// in shared memory; after one cluster barrier (barrier.cluster) lane r of
+// every warp reads CTA r's pair through distributed shared memory (mapa +
+// ld.shared::cluster) and the warp combines them, so that every CTA gets the
+// same M and S = sum_c s_c 2^((m_c - M) log2e).  The store pass scales the
+// held exponentials by exp(m_w - M) / S: one ex2 per key, the row read once.
+//
+// Persistent clusters walk rows; each CTA keeps kClusterDepth rows of its
+// slice in flight (cp.async into shared memory, one commit group per row),
+// refilling a row's slots as soon as they are in registers.  The published
+// CTA pair alternates between two slots by row parity: a partner cannot
+// overwrite slot p (two rows later) before passing the cluster barrier of the
+// row in between, which this CTA reaches only after reading slot p.
+constexpr int kClusterBlock = 512;
+constexpr int kClusterVPT = 4;
+constexpr int kClusterPacks = kClusterBlock * kClusterVPT;  // packs per CTA
+constexpr int kClusterDepth = 1;  // rows of the slice in flight ahead of use (2 measured slower)
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+// The float2 at `local` (this CTA's shared memory) in CTA `rank` of the cluster.
+__device__ __forceinline__ float2 ld_cluster_f2(const float2* local, uint32_t rank) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(local);
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(ra)
+               : "memory");
+  return v;
+}
+
+template <typename TI, typename TO, bool W32>
+__global__ void __launch_bounds__(kClusterBlock, 2)
+softmax_cluster_kernel(const TI* __restrict__ x, int64_t ldx, TO* __restrict__ y, int64_t ldy,
+                       int64_t rows, int nvec) {
+  constexpr int VW = Elem<TI>::kVec;
+  __shared__ float2 wpart[kClusterBlock / 32];
+  __shared__ float2 part[2];
+  extern __shared__ uint4 stage[];  // [kClusterDepth][pack][thread], 32 KB a row
+  const uint32_t rank = cluster_rank(), C = cluster_size();
+  const int64_t first = cluster_id_x(), step = cluster_count_x();
+  const int p0 = (int)rank * kClusterPacks + threadIdx.x;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // one commit group per row, empty past the last row, so that the group of
+  // the row in hand is always the oldest but kClusterDepth - 1
+  const auto issue = [&](int64_t row, int buf) {
+    if (row < rows) {
+      const TI* xr = x + row * ldx;
+      uint4* st = stage + buf * kClusterPacks + threadIdx.x;
+#pragma unroll
+      for (int i = 0; i < kClusterVPT; ++i) {
+        const int p = p0 + i * kClusterBlock;
+        if (p < nvec) cp_async16(st + i * kClusterBlock, xr + (int64_t)p * VW);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int d = 0; d < kClusterDepth; ++d) issue(first + d * step, d);
+  int parity = 0, buf = 0;
+  for (int64_t row = first; row < rows; row += step, parity ^= 1) {
+    uint4 v[kClusterVPT];
+    cp_async_wait_pending<kClusterDepth - 1>();  // (this thread's own copies)
+    const uint4* st = stage + buf * kClusterPacks + threadIdx.x;
+#pragma unroll
+    for (int i = 0; i < kClusterVPT; ++i) {
+      const int p = p0 + i * kClusterBlock;
+      v[i] = p < nvec ? st[i * kClusterBlock] : mask_tail<TI>(make_uint4(0, 0, 0, 0), 0);
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kClusterVPT; ++i) m = fmaxf(m, pack_max<TI>(v[i]));
+    // this thread's slots of `buf` are in registers now: refill them
+    issue(row + kClusterDepth * step, buf);
+    buf = buf + 1 == kClusterDepth ? 0 : buf + 1;
+    // the warp's max, and its exponentials against it kept in registers (an
+    // all -inf warp slice holds zeros and adds nothing)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float e[kClusterVPT][VW];
+    float s = 0.f;
+    const bool live = m != -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kClusterVPT; ++i) {
+      unpack<TI>(v[i], e[i]);
+#pragma unroll
+      for (int k = 0; k < VW; ++k) {
+        e[i][k] = live ? ex2_approx((e[i][k] - m) * kLog2e) : 0.f;
+        s += e[i][k];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) wpart[warp] = make_float2(m, s);
+    __syncthreads();
+    // warp 0 folds the warps' pairs into this CTA's and publishes it; it
+    // reads wpart before its cluster arrive, which every warp's next write to
+    // wpart waits behind
+    if (warp == 0) {
+      const float2 q = lane < kClusterBlock / 32 ? wpart[lane] : make_float2(-INFINITY, 0.f);
+      float mc = q.x;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, o));
+      float sc = q.x != -INFINITY ? q.y * ex2_approx((q.x - mc) * kLog2e) : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+      if (lane == 0) part[parity] = make_float2(mc, sc);
+    }
+    cluster_arrive();
+    cluster_wait();  // every CTA's pair for this row is published
+    // lane r of every warp reads CTA r's pair (C remote loads in flight at
+    // once, not in a row), then the warp combines lanes 0..7
+    const float2 q = lane < C ? ld_cluster_f2(&part[parity], lane)
+                              : make_float2(-INFINITY, 0.f);
+    float M = q.x;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float S = q.x != -INFINITY ? q.y * ex2_approx((q.x - M) * kLog2e) : 0.f;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+    M = __shfl_sync(0xffffffffu, M, 0);
+    S = __shfl_sync(0xffffffffu, S, 0);
+    // exp(x - M) / S = exp(x - m_w) * exp(m_w - M) / S
+    const float scale = ex2_approx((m - M) * kLog2e) * (1.0f / S);
+    TO* yr = y + row * ldy;
+#pragma unroll
+    for (int i = 0; i < kClusterVPT; ++i) {
+      const int p = p0 + i * kClusterBlock;
+      if (p >= nvec) continue;
+#pragma unroll
+      for (int k = 0; k < VW; ++k) e[i][k] *= scale;
+      store_vals<TO, VW, W32>(yr + (int64_t)p * VW, e[i]);
+    }
+  }
+  cp_async_wait_all();
+  // no CTA leaves while a partner may still read its pairs
+  cluster_arrive();
+  cluster_wait();
+}
+
+// Launches the cluster kernel for rows of `nvec` packs, or returns -1 when the
+// row needs more than 8 CTAs or the device cannot place the cluster.
+template <typename TI, typename TO>
+int launch_softmax_cluster(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
+                           int64_t nvec, cudaStream_t stream) {
+  const int C = (int)ceil_div(nvec, kClusterPacks);
+  if (C < 2 || C > 8 || rows * C > 0x7fffffff) return -1;
+  const auto run = [&](auto w32) -> int {
+    constexpr bool W = decltype(w32)::value;
+    auto kern = softmax_cluster_kernel<TI, TO, W>;
+    const size_t smem = (size_t)kClusterDepth * kClusterPacks * sizeof(uint4);
+    // (per launch: the attribute is held per device)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess) {
+      (void)cudaGetLastError();
+      return -1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(rows * C));
+    cfg.blockDim = dim3(kClusterBlock);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1) {
+      (void)cudaGetLastError();
+      return -1;
+    }
+    // persistent: as many clusters as are resident at once, each walking rows
+    cfg.gridDim = dim3((unsigned)(std::min<int64_t>(rows, clusters) * C));
+    (void)cudaLaunchKernelEx(&cfg, kern, x, ldx, y, ldy, rows, (int)nvec);
+    return launch_status();
+  };
+  if constexpr (std::is_same<TO, float>::value && Elem<TI>::kVec == 8) {
+    if (aligned32(y) && ldy % 8 == 0) return run(std::true_type{});
+  }
+  return run(std::false_type{});
+}
+
 template <typename TI, typename TO, bool CAUSAL>
 int launch_softmax(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
                    int64_t cols, int64_t q_len, int64_t offset, cudaStream_t stream) {
@@ -538,7 +753,12 @@ int launch_softmax(const TI* x, int64_t ldx, TO* y, int64_t ldy, int64_t rows,
     }
     if (r < 0) r = row_ladder<8>(nvec, go);
     if (r >= 0) return r;
-    // longer rows: the two-pass kernel
+    // rows too long for one CTA: a cluster of CTAs per row, one pass
+    if constexpr (!CAUSAL) {
+      const int rc = launch_softmax_cluster<TI, TO>(x, ldx, y, ldy, rows, nvec, stream);
+      if (rc >= 0) return rc;
+    }
+    // longer rows, causal rows: the two-pass kernel
     if (nvec > 12288) {
       const int grid = (int)std::min<int64_t>(rows, (int64_t)dev.sm_count);
       softmax_long_kernel<TI, TO, CAUSAL, 1024>

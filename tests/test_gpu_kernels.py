@@ -502,10 +502,12 @@ def test_softmax_f32_out_both_store_widths(causal, cols):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("cols", [40000, 131072, 40001])
+@pytest.mark.parametrize("cols", [40000, 128256, 131072, 40001])
 def test_softmax_long_rows_special_values(dtype, cols):
-    """The two-pass kernel (rows over 4096 packs, both block sizes; 40001
-    columns take the unaligned loop kernel, also two passes) with -inf
+    """Rows over 4096 packs: one thread-block cluster of 3..8 CTAs per row
+    up to 16384 packs (40000, 128256 and 131072 16-bit keys; 40000 fp32
+    keys), the two-pass kernel beyond (131072 fp32 keys), the unaligned
+    loop kernel for 40001 columns (two passes) -- with -inf
     keys, keys far below the max, a one-hot row, a row at the format's
     lowest finite value (fp16 -65504: pass 2 must use the argument pass 1
     summed, else the rounding of m*log2e scales every output by up to
@@ -533,6 +535,25 @@ def test_softmax_long_rows_special_values(dtype, cols):
         got32 = K.softmax(x, out_dtype=torch.float32)
         ref32 = ops.softmax_golden(parity.to_np(x), "f32")
         parity.assert_rel(parity.to_np(got32[ok]), ref32[ok], rtol=1e-5, atol=1e-30)
+
+
+@pytest.mark.parametrize("dtype,cols", [(torch.bfloat16, 128256), (torch.float32, 32000),
+                                        (torch.float16, 50000)])
+def test_softmax_cluster_rows_walk(dtype, cols):
+    """Many more rows than resident clusters: each cluster walks several rows
+    with the next rows' slices in flight, and the last pass of the walk is
+    partial (333 rows)."""
+    dt = parity.dname(dtype)
+    g = torch.Generator().manual_seed(cols)
+    x = (4.0 * torch.randn(333, cols, generator=g)).to(dtype)
+    x[7, : cols // 3] = float("-inf")          # a CTA's whole slice masked
+    xd = x.to(DEV)
+    got = K.softmax(xd)
+    check_float(got, ops.softmax_golden(parity.to_np(xd), dt), dt, f"walk {cols}")
+    if dtype != torch.float32:
+        got32 = K.softmax(xd, out_dtype=torch.float32)
+        ref32 = ops.softmax_golden(parity.to_np(xd), "f32")
+        parity.assert_rel(parity.to_np(got32), ref32, rtol=1e-5, atol=1e-30)
 
 
 def test_softmax_infinities():

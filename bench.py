@@ -443,6 +443,13 @@ def workload_config(args, world):
 
 
 # --------------------------------------------------------------------- main
+def default_e2e_chunks(world):
+    """Token chunks per e2e step.  One rank: 2 (measured on B200, 88.1 ms per
+    step against 89.7 with 4 -- more launches and kernel tails -- and 117
+    with 1)."""
+    return 2
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -459,11 +466,13 @@ def main():
     ap.add_argument("--cpu-reps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    # 2 chunks: measured on B200, 88.1 ms per e2e step against 89.7 with 4
-    # (more chunks, more launches and kernel tails) and 117 with 1
-    ap.add_argument("--e2e-chunks", type=int, default=2,
+    ap.add_argument("--e2e-chunks", type=int, default=0,
                     help="token chunks per e2e step: host->device copies, the layers and the "
-                         "device->host copies of different chunks overlap on three flagos streams")
+                         "device->host copies of different chunks overlap on three flagos "
+                         "streams (0: the per-N default)")
+    ap.add_argument("--e2e-sweep", default="",
+                    help="comma-separated chunk counts to time after the e2e measurement "
+                         "(reported as ms_per_step_by_chunks)")
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--no-hf-e2e", action="store_true",
                     help="skip the HF decoder-model leg (hidden states host -> flagos -> host)")
@@ -669,76 +678,89 @@ def main():
         h_in = torch.empty(T, HIDDEN, dtype=torch.bfloat16, pin_memory=True)
         h_in.copy_(stack.x0)
         h_out = torch.empty_like(h_in, pin_memory=True)
-        chunks = max(1, min(args.e2e_chunks, T))
-        bounds = [(T * c // chunks, T * (c + 1) // chunks) for c in range(chunks)]
         comp = flagos.current_stream(local)
         h2d, d2h = flagos.Stream(local), flagos.Stream(local)
-        # At most two steps in flight: the host waits for step s-2's last
-        # device->host copy before queueing step s, as a serving loop bounds
-        # its queue (device memory then stays at two steps' buffers).
-        inflight = []
-        host_s = [0.0]   # host time spent issuing steps (not waiting on `inflight`)
 
-        def e2e_step():
-            t_issue = time.perf_counter()
-            for lo, hi in bounds:
-                with flagos.stream(h2d):
-                    x_d = h_in[lo:hi].to(fdev, non_blocking=True)
-                    landed = flagos.Event()
-                    landed.record(h2d)
-                comp.wait_event(landed)
-                x_d.record_stream(comp)
-                res = stack.run_flagos(x_d, slice(lo, hi))
-                done = flagos.Event()
-                done.record(comp)
-                d2h.wait_event(done)
-                with flagos.stream(d2h):
-                    h_out[lo:hi].copy_(res, non_blocking=True)
-                res.record_stream(d2h)
-            ev = flagos.Event()
-            ev.record(d2h)
-            inflight.append(ev)
-            host_s[0] += time.perf_counter() - t_issue
-            if len(inflight) > 2:
-                inflight.pop(0).synchronize()
+        def run_e2e(chunks):
+            """Times args.steps e2e steps cut into `chunks` token chunks:
+            (ms for all steps, ms per step of each half, warm-up steps,
+            host issue ms per step), max over ranks."""
+            chunks = max(1, min(chunks, T))
+            bounds = [(T * c // chunks, T * (c + 1) // chunks) for c in range(chunks)]
+            # At most two steps in flight: the host waits for step s-2's last
+            # device->host copy before queueing step s, as a serving loop bounds
+            # its queue (device memory then stays at two steps' buffers).
+            inflight = []
+            host_s = [0.0]   # host time spent issuing steps (not waiting on `inflight`)
 
-        # Warm-up until the flagos allocator's pool has settled: its blocks
-        # are reused only on the stream that freed them and the steps in
-        # flight hold blocks on three streams, so it grows for a while (on
-        # B200 from 8 to about 18 steps, run to run; a step that grows it is
-        # slow on the host).  At least `warmup` steps, then until two steps
-        # in a row leave the pool's reserved bytes unchanged (at most 40).
-        def reserved():  # host-side counter: no synchronisation (steps stay in flight)
-            return flagos.memory_stats().get("pool_reserved", 0)
+            def e2e_step():
+                t_issue = time.perf_counter()
+                for lo, hi in bounds:
+                    with flagos.stream(h2d):
+                        x_d = h_in[lo:hi].to(fdev, non_blocking=True)
+                        landed = flagos.Event()
+                        landed.record(h2d)
+                    comp.wait_event(landed)
+                    x_d.record_stream(comp)
+                    res = stack.run_flagos(x_d, slice(lo, hi))
+                    done = flagos.Event()
+                    done.record(comp)
+                    d2h.wait_event(done)
+                    with flagos.stream(d2h):
+                        h_out[lo:hi].copy_(res, non_blocking=True)
+                    res.record_stream(d2h)
+                ev = flagos.Event()
+                ev.record(d2h)
+                inflight.append(ev)
+                host_s[0] += time.perf_counter() - t_issue
+                if len(inflight) > 2:
+                    inflight.pop(0).synchronize()
 
-        warm, still, last = 0, 0, -1
-        with torch.inference_mode():
-            while warm < 40 and (warm < max(args.warmup, 3) or still < 2):
-                e2e_step()
-                warm += 1
-                now = reserved()
-                still = still + 1 if now == last else 0
-                last = now
-        comp.wait_stream(d2h)
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        em = torch.cuda.Event(enable_timing=True)
-        host_s[0] = 0.0
-        e0.record(comp)
-        with torch.inference_mode():
-            for i in range(args.steps):
-                e2e_step()
-                if i == args.steps // 2 - 1:
-                    em.record(comp)    # the first half's layers are queued before em
-        comp.wait_stream(d2h)          # the last chunk is in host memory at e1
-        e1.record(comp)
-        torch.cuda.synchronize()
-        ems = sharding.max_over_ranks(e0.elapsed_time(e1), dev)
-        halves = [ems / args.steps] * 2
-        if args.steps >= 2:
-            halves = [sharding.max_over_ranks(e0.elapsed_time(em), dev) / (args.steps // 2),
-                      sharding.max_over_ranks(em.elapsed_time(e1), dev)
-                      / (args.steps - args.steps // 2)]
+            # Warm-up until the flagos allocator's pool has settled: its blocks
+            # are reused only on the stream that freed them and the steps in
+            # flight hold blocks on three streams, so it grows for a while (on
+            # B200 from 8 to about 18 steps, run to run; a step that grows it is
+            # slow on the host).  At least `warmup` steps, then until two steps
+            # in a row leave the pool's reserved bytes unchanged (at most 40).
+            def reserved():  # host-side counter: no synchronisation (steps stay in flight)
+                return flagos.memory_stats().get("pool_reserved", 0)
+
+            warm, still, last = 0, 0, -1
+            with torch.inference_mode():
+                while warm < 40 and (warm < max(args.warmup, 3) or still < 2):
+                    e2e_step()
+                    warm += 1
+                    now = reserved()
+                    still = still + 1 if now == last else 0
+                    last = now
+            comp.wait_stream(d2h)
+            barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            em = torch.cuda.Event(enable_timing=True)
+            host_s[0] = 0.0
+            e0.record(comp)
+            with torch.inference_mode():
+                for i in range(args.steps):
+                    e2e_step()
+                    if i == args.steps // 2 - 1:
+                        em.record(comp)    # the first half's layers are queued before em
+            comp.wait_stream(d2h)          # the last chunk is in host memory at e1
+            e1.record(comp)
+            torch.cuda.synchronize()
+            ems = sharding.max_over_ranks(e0.elapsed_time(e1), dev)
+            halves = [ems / args.steps] * 2
+            if args.steps >= 2:
+                halves = [sharding.max_over_ranks(e0.elapsed_time(em), dev) / (args.steps // 2),
+                          sharding.max_over_ranks(em.elapsed_time(e1), dev)
+                          / (args.steps - args.steps // 2)]
+            host_ms = sharding.max_over_ranks(host_s[0] * 1e3, dev) / args.steps
+            return ems, halves, warm, host_ms
+
+        chunks = max(1, min(args.e2e_chunks or default_e2e_chunks(world), T))
+        ems, halves, warm, host_ms = run_e2e(chunks)
+        by_chunks = {}
+        for c in sorted({int(v) for v in args.e2e_sweep.split(",") if v}):
+            by_chunks[c] = round(run_e2e(c)[0] / args.steps, 3)
         # the e2e result equals the device-resident path's result
         same = bool(torch.equal(h_out.to(dev), stack.run(stack.x0)))
         nbytes = h_in.numel() * h_in.element_size()
@@ -787,10 +809,10 @@ def main():
                "ms_per_step": ems / args.steps, "matches_device_path": same,
                "chunks": chunks, "host_copy_gbs": rates,
                "ms_per_step_halves": [round(h, 3) for h in halves],
+               **({"ms_per_step_by_chunks": by_chunks} if by_chunks else {}),
                "warmup_steps": warm,
                "copy_floor_ms": round(floor, 3),
-               "host_issue_ms_per_step": round(
-                   sharding.max_over_ranks(host_s[0] * 1e3, dev) / args.steps, 3),
+               "host_issue_ms_per_step": round(host_ms, 3),
                "copy_floor_what": "one step's host->device and device->host copies at the same "
                                   "time on two streams, all ranks at once (max over ranks)",
                "api": "torch_fl.ops (flagos:: ops) on flagos tensors under "

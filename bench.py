@@ -738,16 +738,24 @@ def main():
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             em = torch.cuda.Event(enable_timing=True)
             host_s[0] = 0.0
+            marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+            hmarks = []
             e0.record(comp)
+            t0 = time.perf_counter()
             with torch.inference_mode():
                 for i in range(args.steps):
                     e2e_step()
+                    marks[i].record(comp)  # step i's layers are done at marks[i]
+                    hmarks.append(time.perf_counter() - t0)  # step i queued on the host
                     if i == args.steps // 2 - 1:
                         em.record(comp)    # the first half's layers are queued before em
             comp.wait_stream(d2h)          # the last chunk is in host memory at e1
             e1.record(comp)
             torch.cuda.synchronize()
             ems = sharding.max_over_ranks(e0.elapsed_time(e1), dev)
+            # device time from the start to each step's last layer (max over ranks)
+            each[:] = [round(sharding.max_over_ranks(e0.elapsed_time(m), dev), 3) for m in marks]
+            heach[:] = [round(sharding.max_over_ranks(h * 1e3, dev), 3) for h in hmarks]
             halves = [ems / args.steps] * 2
             if args.steps >= 2:
                 halves = [sharding.max_over_ranks(e0.elapsed_time(em), dev) / (args.steps // 2),
@@ -757,7 +765,9 @@ def main():
             return ems, halves, warm, host_ms
 
         chunks = max(1, min(args.e2e_chunks or default_e2e_chunks(world), T))
+        each, heach = [], []
         ems, halves, warm, host_ms = run_e2e(chunks)
+        layers_done_ms, queued_ms = list(each), list(heach)
         by_chunks = {}
         for c in sorted({int(v) for v in args.e2e_sweep.split(",") if v}):
             by_chunks[c] = round(run_e2e(c)[0] / args.steps, 3)
@@ -810,6 +820,8 @@ def main():
                "chunks": chunks, "host_copy_gbs": rates,
                "ms_per_step_halves": [round(h, 3) for h in halves],
                **({"ms_per_step_by_chunks": by_chunks} if by_chunks else {}),
+               "layers_done_ms": layers_done_ms,
+               "host_queued_ms": queued_ms,
                "warmup_steps": warm,
                "copy_floor_ms": round(floor, 3),
                "host_issue_ms_per_step": round(host_ms, 3),

@@ -731,6 +731,7 @@ def main():
                     e2e_step()
                     warm += 1
                     now = reserved()
+                    pool_warm.append(now)
                     still = still + 1 if now == last else 0
                     last = now
             comp.wait_stream(d2h)
@@ -747,6 +748,7 @@ def main():
                     e2e_step()
                     marks[i].record(comp)  # step i's layers are done at marks[i]
                     hmarks.append(time.perf_counter() - t0)  # step i queued on the host
+                    pool_timed.append(reserved())
                     if i == args.steps // 2 - 1:
                         em.record(comp)    # the first half's layers are queued before em
             comp.wait_stream(d2h)          # the last chunk is in host memory at e1
@@ -765,8 +767,11 @@ def main():
             return ems, halves, warm, host_ms
 
         chunks = max(1, min(args.e2e_chunks or default_e2e_chunks(world), T))
-        each, heach = [], []
+        each, heach, pool_warm, pool_timed = [], [], [], []
         ems, halves, warm, host_ms = run_e2e(chunks)
+        # (warm-up: this rank's, its length differs by rank; timed: max over ranks)
+        pool_mb = {"warm_up": [round(v / 2**20) for v in pool_warm],
+                   "timed": [round(sharding.max_over_ranks(v, dev) / 2**20) for v in pool_timed]}
         layers_done_ms, queued_ms = list(each), list(heach)
         by_chunks = {}
         for c in sorted({int(v) for v in args.e2e_sweep.split(",") if v}):
@@ -822,6 +827,7 @@ def main():
                **({"ms_per_step_by_chunks": by_chunks} if by_chunks else {}),
                "layers_done_ms": layers_done_ms,
                "host_queued_ms": queued_ms,
+               "pool_reserved_mb_after_each_step": pool_mb,
                "warmup_steps": warm,
                "copy_floor_ms": round(floor, 3),
                "host_issue_ms_per_step": round(host_ms, 3),

@@ -720,14 +720,15 @@ def main():
             # are reused only on the stream that freed them and the steps in
             # flight hold blocks on three streams, so it grows for a while (on
             # B200 from 8 to about 18 steps, run to run; a step that grows it is
-            # slow on the host).  At least `warmup` steps, then until two steps
-            # in a row leave the pool's reserved bytes unchanged (at most 40).
+            # slow on the host).  At least `warmup` and 12 steps, then until
+            # three steps in a row leave the pool's reserved bytes unchanged
+            # (at most 40).
             def reserved():  # host-side counter: no synchronisation (steps stay in flight)
                 return flagos.memory_stats().get("pool_reserved", 0)
 
             warm, still, last = 0, 0, -1
             with torch.inference_mode():
-                while warm < 40 and (warm < max(args.warmup, 3) or still < 2):
+                while warm < 40 and (warm < max(args.warmup, 12) or still < 3):
                     e2e_step()
                     warm += 1
                     now = reserved()
